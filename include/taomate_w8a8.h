@@ -1,0 +1,179 @@
+/*
+ * taomate_w8a8.h -- C ABI of the B200 (sm_100a) selective-W8A8 linear path.
+ *
+ * Plain pointers, sizes and a CUDA stream passed as `void*` (a cudaStream_t;
+ * NULL means the legacy default stream).  All pointers are device pointers
+ * unless stated otherwise.  Nothing here allocates device memory, retains a
+ * pointer after returning, or synchronises the stream.  Every function
+ * returns a tm_status code; argument errors are detected on the host before
+ * any launch.  Wait timeouts inside kernels are recorded in a per-device
+ * status word read with tm_device_status().
+ *
+ * The reference (TaoMate-HD) reaches this path through two vLLM operators:
+ *   torch.ops._C.dynamic_scaled_int8_quant(out, input, scales, azp)
+ *       src/taomate_hd/inference/w8a8.py:71   (workspace path)
+ *       src/taomate_hd/inference/w8a8.py:141  (vllm._custom_ops.scaled_int8_quant)
+ *   torch.ops._C.cutlass_scaled_mm(out, a, b, scale_a, scale_b, bias)
+ *       src/taomate_hd/inference/w8a8.py:72   (workspace path)
+ *       src/taomate_hd/inference/w8a8.py:142  (vllm._custom_ops.cutlass_scaled_mm)
+ * Weight conversion is src/taomate_hd/inference/w8a8.py:175-179 and the
+ * adaLN producers are src/taomate_hd/inference/fused_kernels.py:220-236 and
+ * :322-347.
+ */
+#ifndef TAOMATE_W8A8_H
+#define TAOMATE_W8A8_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define TM_OK 0
+#define TM_ERR_NULL_POINTER 1     /* a required pointer is NULL */
+#define TM_ERR_SHAPE 2            /* negative / inconsistent sizes or strides */
+#define TM_ERR_ALIGNMENT 3        /* pointer or stride alignment not met */
+#define TM_ERR_DTYPE 4            /* unsupported dtype code */
+#define TM_ERR_UNSUPPORTED 5      /* valid request this build does not implement */
+#define TM_ERR_CUDA 6             /* a CUDA runtime call failed */
+#define TM_ERR_DEVICE_TIMEOUT 7   /* a kernel wait gave up (tm_device_status) */
+#define TM_ERR_TOO_LARGE 8        /* size exceeds a documented maximum */
+
+/* ---- dtype codes ------------------------------------------------------- */
+#define TM_DTYPE_BF16 0
+#define TM_DTYPE_FP16 1
+#define TM_DTYPE_FP32 2
+
+/* ---- GEMM epilogue flags (tm_scaled_mm_i8_ex) -------------------------- */
+/* gelu_tanh applied to the rounded output: y = round(gelu(round(x)))      */
+#define TM_EPI_GELU_TANH 0x1u
+
+/* Human-readable text for a status code (static storage). */
+const char* tm_status_string(int status);
+
+/* Library version, major * 10000 + minor * 100 + patch. */
+int tm_version(void);
+
+/*
+ * Read (and optionally clear) the device status word of `device`: 0 when no
+ * kernel of this library has recorded an error since the last clear,
+ * otherwise a device status (1 = wait timeout, 2 = drain timeout).
+ * Synchronises the device.
+ */
+int tm_device_status(int device, int* code, int clear);
+
+/*
+ * Dynamic per-token symmetric int8 quantisation.
+ * Replaces torch.ops._C.dynamic_scaled_int8_quant(out, input, scales, azp)
+ * (src/taomate_hd/inference/w8a8.py:71) and the dynamic branch of
+ * vllm._custom_ops.scaled_int8_quant (src/taomate_hd/inference/w8a8.py:141).
+ * For each row r of input[rows, cols] (row stride `input_row_stride`
+ * elements):
+ *   amax      = max_k |x[r,k]|                 (fp32)
+ *   scales[r] = amax / 127                      (fp32, IEEE division)
+ *   inv       = amax == 0 ? 0 : 127 / amax      (fp32, IEEE division)
+ *   out[r,k]  = sat_int8(round_half_even(x[r,k] * inv))
+ * out is [rows, cols] contiguous int8; scales is [rows] fp32.
+ * azp must be NULL (asymmetric quantisation is not used by the reference).
+ */
+int tm_dynamic_scaled_int8_quant(int8_t* out, const void* input, int input_dtype,
+                                 float* scales, int32_t* azp, int64_t rows, int64_t cols,
+                                 int64_t input_row_stride, void* stream);
+
+/*
+ * Static per-tensor symmetric int8 quantisation with a device-resident fp32
+ * scale[0]: out = sat_int8(round_half_even(x / scale)).
+ * Replaces torch.ops._C.static_scaled_int8_quant, the static branch of
+ * vllm._custom_ops.scaled_int8_quant (the reference calls it only with
+ * scale=None, src/taomate_hd/inference/w8a8.py:141).
+ */
+int tm_static_scaled_int8_quant(int8_t* out, const void* input, int input_dtype,
+                                const float* scale, int32_t* azp, int64_t rows, int64_t cols,
+                                int64_t input_row_stride, void* stream);
+
+/*
+ * Scaled int8 GEMM with bf16/fp16 output.
+ * Replaces torch.ops._C.cutlass_scaled_mm(out, a, b, scale_a, scale_b, bias)
+ * (src/taomate_hd/inference/w8a8.py:72, :142-144).
+ *   out[m,n] = cvt(scale_a[m] * (scale_b[n] * float(sum_k a[m,k] * b[k,n])) (+ bias[n]))
+ * a: int8 [m, k] row-major, row stride lda (elements, multiple of 16).
+ * b: int8 [k, n] column-major, i.e. the [n, k] row-major weight storage,
+ *    column stride ldb (multiple of 16) -- the `weight.t()` view.
+ * scale_a: fp32, numel 1 (per-tensor) or m (per-token).
+ * scale_b: fp32, numel 1 (per-tensor) or n (per-channel).
+ * bias: NULL or [n] in out_dtype.  out: [m, n] row-major, row stride ldo.
+ * Requires k % 16 == 0 and n % 16 == 0 (the same contract as vLLM's CUTLASS
+ * path), 16-byte aligned a/b/out.
+ */
+int tm_cutlass_scaled_mm(void* out, int out_dtype, const int8_t* a, const int8_t* b,
+                         const float* scale_a, int64_t scale_a_numel, const float* scale_b,
+                         int64_t scale_b_numel, const void* bias, int64_t m, int64_t n,
+                         int64_t k, int64_t lda, int64_t ldb, int64_t ldo, void* stream);
+
+/*
+ * tm_cutlass_scaled_mm plus fused epilogue options (TM_EPI_* flags) and an
+ * optional raw int32 accumulator output acc_debug[m, n] (row stride n), which
+ * exposes the exact int32 sums for bit-exact checking.
+ * Extends cutlass_scaled_mm for the BASELINE fc1 epilogue (bias + gelu_tanh);
+ * no single reference call site.
+ */
+int tm_scaled_mm_i8_ex(void* out, int out_dtype, const int8_t* a, const int8_t* b,
+                       const float* scale_a, int64_t scale_a_numel, const float* scale_b,
+                       int64_t scale_b_numel, const void* bias, int64_t m, int64_t n,
+                       int64_t k, int64_t lda, int64_t ldb, int64_t ldo, uint32_t epilogue,
+                       int32_t* acc_debug, void* stream);
+
+/*
+ * tm_scaled_mm_i8_ex with a forced N-tile width (256, 128 or 64) instead of
+ * the size heuristic; lets tests cover every kernel instantiation.  Same
+ * reference counterpart as tm_cutlass_scaled_mm.
+ */
+int tm_scaled_mm_i8_tile(void* out, int out_dtype, const int8_t* a, const int8_t* b,
+                         const float* scale_a, int64_t scale_a_numel, const float* scale_b,
+                         int64_t scale_b_numel, const void* bias, int64_t m, int64_t n,
+                         int64_t k, int64_t lda, int64_t ldb, int64_t ldo, uint32_t epilogue,
+                         int32_t* acc_debug, int tile_n, void* stream);
+
+/*
+ * Per-output-channel symmetric weight quantisation, bit-exact with
+ * _quantize_cutlass_w8a8_weight (src/taomate_hd/inference/w8a8.py:175-179):
+ *   scales[n] = max(float(max_k |w[n,k]|) / 127, 1e-12)
+ *   q[n,k]    = clamp(round_half_even(float(w[n,k]) / scales[n]), -127, 127)
+ * w: [n, k] row-major (row stride k) in w_dtype; q: [n, k]; scales: [n].
+ */
+int tm_quantize_weight_int8(int8_t* q, float* scales, const void* w, int w_dtype, int64_t n,
+                            int64_t k, void* stream);
+
+/*
+ * adaLN modulate fused into the dynamic per-token quantisation.
+ * Follows _modulate_kernel (src/taomate_hd/inference/fused_kernels.py:220-236):
+ *   t    = index ? index[r] : r
+ *   h    = bf16(bf16(x[r,c] * bf16(1 + scale[t,c])) + shift[t,c])
+ * then h is quantised exactly as tm_dynamic_scaled_int8_quant.  x, shift,
+ * scale and hidden_out are bf16; shift/scale rows have stride table_stride.
+ * hidden_out (optional, NULL to skip) receives h as [rows, cols] bf16.
+ */
+int tm_modulate_int8_quant(int8_t* out, float* scales, void* hidden_out, const void* x,
+                           const void* shift, const void* scale, const int64_t* index,
+                           int64_t table_stride, int64_t rows, int64_t cols, void* stream);
+
+/*
+ * RMSNorm + adaLN modulate fused into the dynamic per-token quantisation.
+ * Follows _rms_norm_modulate_kernel
+ * (src/taomate_hd/inference/fused_kernels.py:322-347):
+ *   n = bf16(x * rsqrt(mean(x^2) + eps) * weight)
+ *   h = bf16(bf16(n * bf16(1 + scale[t])) + shift[t])
+ * then quantised as tm_dynamic_scaled_int8_quant.  All tensors bf16.
+ */
+int tm_rms_norm_modulate_int8_quant(int8_t* out, float* scales, void* hidden_out,
+                                    const void* x, const void* norm_weight, float eps,
+                                    const void* shift, const void* scale, const int64_t* index,
+                                    int64_t table_stride, int64_t rows, int64_t cols,
+                                    void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TAOMATE_W8A8_H */

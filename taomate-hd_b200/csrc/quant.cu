@@ -1,0 +1,490 @@
+// Row-wise int8 quantisation kernels (sm_100a).
+//
+//   * dynamic per-token symmetric quant   -> vLLM dynamic_scaled_int8_quant
+//   * static per-tensor symmetric quant   -> vLLM static_scaled_int8_quant
+//   * per-output-channel weight quant     -> w8a8.py:175-179
+//   * adaLN modulate + quant              -> fused_kernels.py:220-236 feeding w8a8.py:71
+//   * RMSNorm + modulate + quant          -> fused_kernels.py:322-347 feeding w8a8.py:71
+//
+// Design: a "row group" of TPR threads (32..256, a power of two) owns one
+// row.  Each thread issues all of its 16-byte loads up front (VPT vectors,
+// strided by TPR so each warp-wide load is one contiguous 512-byte span),
+// keeps the values in registers, reduces |x| max with warp shuffles (plus a
+// shared-memory step when the group spans several warps) and writes int8 +
+// the fp32 scale: one HBM read of the activations, one write of int8.
+// Rows whose width is not a multiple of the vector or whose base is not
+// 16-byte aligned take a two-pass scalar kernel (one block per row).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "common.h"
+
+namespace tmw {
+namespace {
+
+enum QuantMode : int {
+  kDynamic = 0,    // per-row amax/127
+  kStatic = 1,     // given per-tensor scale, q = x / s
+  kWeight = 2,     // per-row amax/127 clamped at 1e-12, q = clamp(x / s, +-127)
+  kModulate = 3,   // adaLN modulate, then dynamic
+  kRmsModulate = 4 // RMSNorm, adaLN modulate, then dynamic
+};
+
+struct QuantParams {
+  const void* x;
+  int64_t ldx;
+  int8_t* q;          // [rows, cols], row stride cols
+  float* scales;      // [rows]
+  const float* static_scale;
+  __nv_bfloat16* hidden_out;  // optional [rows, cols] bf16 (modulate modes)
+  const __nv_bfloat16* shift;
+  const __nv_bfloat16* mod_scale;
+  const int64_t* index;
+  int64_t table_stride;
+  const __nv_bfloat16* norm_w;
+  float eps;
+  int64_t rows;
+  int64_t cols;
+  int tpr_log2;
+};
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half v) {
+  return __half2float(v);
+}
+template <>
+__device__ __forceinline__ float to_f32<float>(float v) {
+  return v;
+}
+
+// Round-to-nearest-even through bf16 and back (identical to the reference's
+// _round_bf16 for finite values, fused_kernels.py:57-61).
+__device__ __forceinline__ float round_bf16(float v) {
+  return __bfloat162float(__float2bfloat16_rn(v));
+}
+
+// Saturating round-half-even float -> int8 (NaN -> 0).
+__device__ __forceinline__ int f2i8_rn_sat(float x) {
+  int r;
+  asm("cvt.rni.sat.s8.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+template <typename T>
+struct VecTraits {
+  static constexpr int kElems = 16 / sizeof(T);
+};
+
+// Unpack one 16-byte vector into floats.
+template <typename T>
+__device__ __forceinline__ void unpack16(const uint4& raw, float (&out)[VecTraits<T>::kElems]) {
+  const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+  for (int j = 0; j < VecTraits<T>::kElems; ++j) out[j] = to_f32<T>(e[j]);
+}
+
+__device__ __forceinline__ uint4 ld_stream16(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ uint4 ld_cached16(const void* p) {
+  return __ldg(reinterpret_cast<const uint4*>(p));
+}
+
+// Max / sum over the TPR threads of a row group.  Groups of <= 32 threads
+// live inside one warp; wider groups combine per-warp partials through
+// shared memory (every thread of the block reaches the __syncthreads).
+template <bool kMax>
+__device__ __forceinline__ float group_reduce(float v, int tpr, float* red) {
+  const int lane_span = tpr < 32 ? tpr : 32;
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    if (off < lane_span) {
+      const float o = __shfl_xor_sync(0xffffffffu, v, off);
+      v = kMax ? fmaxf(v, o) : v + o;
+    }
+  }
+  if (tpr > 32) {
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    __syncthreads();  // protect `red` from the previous use
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    const int wpr = tpr >> 5;
+    const int first = (warp / wpr) * wpr;
+    float acc = red[first];
+    for (int w = 1; w < wpr; ++w) acc = kMax ? fmaxf(acc, red[first + w]) : acc + red[first + w];
+    v = acc;
+  }
+  return v;
+}
+
+template <typename T, int VPT, int MODE>
+__global__ void __launch_bounds__(256) quant_rows_kernel(const QuantParams p) {
+  constexpr int E = VecTraits<T>::kElems;
+  __shared__ float red[8];
+  const int tpr = 1 << p.tpr_log2;
+  const int local_row = threadIdx.x >> p.tpr_log2;
+  const int t = threadIdx.x & (tpr - 1);
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> p.tpr_log2) + local_row;
+  const bool active = row < p.rows;
+  const int64_t nvec = p.cols / E;
+  const T* xr = reinterpret_cast<const T*>(p.x) + (active ? row : 0) * p.ldx;
+
+  float v[VPT][E];
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int64_t vi = t + static_cast<int64_t>(i) * tpr;
+    if (active && vi < nvec) {
+      unpack16<T>(ld_stream16(xr + vi * E), v[i]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < E; ++j) v[i][j] = 0.f;
+    }
+  }
+
+  if constexpr (MODE == kRmsModulate) {
+    // variance = sum(x^2) / cols ; n = bf16(x * rsqrt(variance + eps) * w)
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i)
+#pragma unroll
+      for (int j = 0; j < E; ++j) ss = __fadd_rn(ss, __fmul_rn(v[i][j], v[i][j]));
+    ss = group_reduce<false>(ss, tpr, red);
+    const float variance = __fdiv_rn(ss, static_cast<float>(p.cols));
+    const float rinv = rsqrtf(__fadd_rn(variance, p.eps));
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int64_t vi = t + static_cast<int64_t>(i) * tpr;
+      if (active && vi < nvec) {
+        float w[E];
+        unpack16<__nv_bfloat16>(ld_cached16(p.norm_w + vi * E), w);
+#pragma unroll
+        for (int j = 0; j < E; ++j) v[i][j] = round_bf16(__fmul_rn(__fmul_rn(v[i][j], rinv), w[j]));
+      }
+    }
+  }
+
+  if constexpr (MODE == kModulate || MODE == kRmsModulate) {
+    // h = bf16(bf16(x * bf16(1 + scale[t])) + shift[t])
+    const int64_t trow = active ? (p.index ? p.index[row] : row) : 0;
+    const __nv_bfloat16* sc_row = p.mod_scale + trow * p.table_stride;
+    const __nv_bfloat16* sh_row = p.shift + trow * p.table_stride;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int64_t vi = t + static_cast<int64_t>(i) * tpr;
+      if (active && vi < nvec) {
+        float sc[E], sh[E];
+        unpack16<__nv_bfloat16>(ld_stream16(sc_row + vi * E), sc);
+        unpack16<__nv_bfloat16>(ld_stream16(sh_row + vi * E), sh);
+#pragma unroll
+        for (int j = 0; j < E; ++j) {
+          const float m = round_bf16(__fmul_rn(v[i][j], round_bf16(__fadd_rn(1.0f, sc[j]))));
+          v[i][j] = round_bf16(__fadd_rn(m, sh[j]));
+        }
+        if (p.hidden_out != nullptr) {
+          uint4 packed;
+          __nv_bfloat162* hp = reinterpret_cast<__nv_bfloat162*>(&packed);
+#pragma unroll
+          for (int j = 0; j < E / 2; ++j) hp[j] = __floats2bfloat162_rn(v[i][2 * j], v[i][2 * j + 1]);
+          *reinterpret_cast<uint4*>(p.hidden_out + row * p.cols + vi * E) = packed;
+        }
+      }
+    }
+  }
+
+  float inv;
+  if constexpr (MODE == kStatic) {
+    inv = 0.f;  // unused: static mode divides by the given scale
+  } else {
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i)
+#pragma unroll
+      for (int j = 0; j < E; ++j) amax = fmaxf(amax, fabsf(v[i][j]));
+    amax = group_reduce<true>(amax, tpr, red);
+    if constexpr (MODE == kWeight) {
+      const float s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-12f);
+      if (active && t == 0) p.scales[row] = s;
+      inv = s;  // weight mode divides by the clamped scale
+    } else {
+      if (active && t == 0) p.scales[row] = __fdiv_rn(amax, 127.0f);
+      inv = amax == 0.f ? 0.f : __fdiv_rn(127.0f, amax);
+    }
+  }
+  const float static_s = MODE == kStatic ? *p.static_scale : 0.f;
+
+  if (!active) return;
+  int8_t* qr = p.q + row * p.cols;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int64_t vi = t + static_cast<int64_t>(i) * tpr;
+    if (vi < nvec) {
+      uint32_t packed[E / 4];
+#pragma unroll
+      for (int w = 0; w < E / 4; ++w) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          const float xv = v[i][4 * w + b];
+          int qi;
+          if constexpr (MODE == kStatic) {
+            qi = f2i8_rn_sat(__fdiv_rn(xv, static_s));
+          } else if constexpr (MODE == kWeight) {
+            qi = f2i8_rn_sat(__fdiv_rn(xv, inv));
+            qi = qi < -127 ? -127 : qi;
+          } else {
+            qi = f2i8_rn_sat(__fmul_rn(xv, inv));
+          }
+          word |= (static_cast<uint32_t>(qi) & 0xffu) << (8 * b);
+        }
+        packed[w] = word;
+      }
+      if constexpr (E == 8) {
+        *reinterpret_cast<uint2*>(qr + vi * E) = make_uint2(packed[0], packed[1]);
+      } else {
+        *reinterpret_cast<uint32_t*>(qr + vi * E) = packed[0];
+      }
+    }
+  }
+}
+
+// Two-pass scalar fallback: any width, any alignment.  One block per row.
+template <typename T, int MODE>
+__global__ void __launch_bounds__(256) quant_rows_scalar_kernel(const QuantParams p) {
+  __shared__ float red[8];
+  const int64_t row = blockIdx.x;
+  if (row >= p.rows) return;
+  const T* xr = reinterpret_cast<const T*>(p.x) + row * p.ldx;
+  float inv = 0.f;
+  float s_use = 0.f;
+  if constexpr (MODE == kStatic) {
+    s_use = *p.static_scale;
+  } else {
+    float amax = 0.f;
+    for (int64_t c = threadIdx.x; c < p.cols; c += blockDim.x) amax = fmaxf(amax, fabsf(to_f32<T>(xr[c])));
+    amax = group_reduce<true>(amax, 256, red);
+    if constexpr (MODE == kWeight) {
+      s_use = fmaxf(__fdiv_rn(amax, 127.0f), 1e-12f);
+      if (threadIdx.x == 0) p.scales[row] = s_use;
+    } else {
+      if (threadIdx.x == 0) p.scales[row] = __fdiv_rn(amax, 127.0f);
+      inv = amax == 0.f ? 0.f : __fdiv_rn(127.0f, amax);
+    }
+  }
+  int8_t* qr = p.q + row * p.cols;
+  for (int64_t c = threadIdx.x; c < p.cols; c += blockDim.x) {
+    const float xv = to_f32<T>(xr[c]);
+    int qi;
+    if constexpr (MODE == kStatic) {
+      qi = f2i8_rn_sat(__fdiv_rn(xv, s_use));
+    } else if constexpr (MODE == kWeight) {
+      qi = f2i8_rn_sat(__fdiv_rn(xv, s_use));
+      qi = qi < -127 ? -127 : qi;
+    } else {
+      qi = f2i8_rn_sat(__fmul_rn(xv, inv));
+    }
+    qr[c] = static_cast<int8_t>(qi);
+  }
+}
+
+// ------------------------------------------------------------------ host
+constexpr int kMaxVpt = 16;
+
+// Pick threads-per-row (power of two, 32..256) and vectors-per-thread.
+bool pick_layout(int64_t nvec, int* tpr_log2, int* vpt) {
+  for (int l = 5; l <= 8; ++l) {
+    const int64_t v = (nvec + (1 << l) - 1) >> l;
+    if (v <= 8 || (l == 8 && v <= kMaxVpt)) {
+      *tpr_log2 = l;
+      *vpt = static_cast<int>(v);
+      return true;
+    }
+  }
+  return false;
+}
+
+// Round vpt up to an instantiated value.
+int round_vpt(int v) {
+  static const int kSet[] = {1, 2, 3, 4, 6, 8, 12, 16};
+  for (int s : kSet)
+    if (v <= s) return s;
+  return -1;
+}
+
+template <typename T, int MODE>
+int launch_vec(const QuantParams& base, int tpr_log2, int vpt, cudaStream_t stream) {
+  QuantParams p = base;
+  p.tpr_log2 = tpr_log2;
+  const int rpb = 256 >> tpr_log2;
+  const int64_t grid = (p.rows + rpb - 1) / rpb;
+  if (grid > 0x7fffffffLL) return TM_ERR_TOO_LARGE;
+  const dim3 g(static_cast<unsigned>(grid));
+  switch (round_vpt(vpt)) {
+    case 1: quant_rows_kernel<T, 1, MODE><<<g, 256, 0, stream>>>(p); break;
+    case 2: quant_rows_kernel<T, 2, MODE><<<g, 256, 0, stream>>>(p); break;
+    case 3: quant_rows_kernel<T, 3, MODE><<<g, 256, 0, stream>>>(p); break;
+    case 4: quant_rows_kernel<T, 4, MODE><<<g, 256, 0, stream>>>(p); break;
+    case 6: quant_rows_kernel<T, 6, MODE><<<g, 256, 0, stream>>>(p); break;
+    case 8: quant_rows_kernel<T, 8, MODE><<<g, 256, 0, stream>>>(p); break;
+    case 12: quant_rows_kernel<T, 12, MODE><<<g, 256, 0, stream>>>(p); break;
+    case 16: quant_rows_kernel<T, 16, MODE><<<g, 256, 0, stream>>>(p); break;
+    default: return TM_ERR_UNSUPPORTED;
+  }
+  return check_launch();
+}
+
+template <typename T, int MODE>
+int launch_quant_typed(const QuantParams& p, cudaStream_t stream) {
+  constexpr int E = VecTraits<T>::kElems;
+  int tpr_log2 = 0, vpt = 0;
+  const bool vec_ok = (p.cols % E == 0) && (p.ldx % E == 0) && aligned16(p.x) &&
+                      aligned16(p.q) && pick_layout(p.cols / E, &tpr_log2, &vpt);
+  if (vec_ok) return launch_vec<T, MODE>(p, tpr_log2, vpt, stream);
+  if (p.rows > 0x7fffffffLL) return TM_ERR_TOO_LARGE;
+  quant_rows_scalar_kernel<T, MODE><<<static_cast<unsigned>(p.rows), 256, 0, stream>>>(p);
+  return check_launch();
+}
+
+template <int MODE>
+int launch_quant(const QuantParams& p, int dtype, cudaStream_t stream) {
+  switch (dtype) {
+    case TM_DTYPE_BF16: return launch_quant_typed<__nv_bfloat16, MODE>(p, stream);
+    case TM_DTYPE_FP16: return launch_quant_typed<__half, MODE>(p, stream);
+    case TM_DTYPE_FP32: return launch_quant_typed<float, MODE>(p, stream);
+    default: return TM_ERR_DTYPE;
+  }
+}
+
+int check_rows_cols(int64_t rows, int64_t cols, int64_t ld) {
+  if (rows < 0 || cols <= 0) return TM_ERR_SHAPE;
+  if (ld < cols) return TM_ERR_SHAPE;
+  return TM_OK;
+}
+
+template <int MODE>
+int launch_modulate(QuantParams p, cudaStream_t stream) {
+  // Modulate modes need the vector layout (bf16, width % 8, aligned rows).
+  if (p.cols % 8 != 0 || p.table_stride % 8 != 0 || !aligned16(p.x) || !aligned16(p.q) ||
+      !aligned16(p.shift) || !aligned16(p.mod_scale) ||
+      (p.hidden_out != nullptr && !aligned16(p.hidden_out)) ||
+      (MODE == kRmsModulate && !aligned16(p.norm_w)))
+    return TM_ERR_ALIGNMENT;
+  int tpr_log2 = 0, vpt = 0;
+  if (!pick_layout(p.cols / 8, &tpr_log2, &vpt)) return TM_ERR_TOO_LARGE;
+  return launch_vec<__nv_bfloat16, MODE>(p, tpr_log2, vpt, stream);
+}
+
+}  // namespace
+}  // namespace tmw
+
+extern "C" {
+
+int tm_dynamic_scaled_int8_quant(int8_t* out, const void* input, int input_dtype, float* scales,
+                                 int32_t* azp, int64_t rows, int64_t cols,
+                                 int64_t input_row_stride, void* stream) {
+  if (azp != nullptr) return TM_ERR_UNSUPPORTED;
+  if (int s = tmw::check_rows_cols(rows, cols, input_row_stride)) return s;
+  if (rows == 0) return TM_OK;
+  if (!out || !input || !scales) return TM_ERR_NULL_POINTER;
+  tmw::QuantParams p{};
+  p.x = input;
+  p.ldx = input_row_stride;
+  p.q = out;
+  p.scales = scales;
+  p.rows = rows;
+  p.cols = cols;
+  return tmw::launch_quant<tmw::kDynamic>(p, input_dtype, tmw::as_stream(stream));
+}
+
+int tm_static_scaled_int8_quant(int8_t* out, const void* input, int input_dtype,
+                                const float* scale, int32_t* azp, int64_t rows, int64_t cols,
+                                int64_t input_row_stride, void* stream) {
+  if (azp != nullptr) return TM_ERR_UNSUPPORTED;
+  if (int s = tmw::check_rows_cols(rows, cols, input_row_stride)) return s;
+  if (rows == 0) return TM_OK;
+  if (!out || !input || !scale) return TM_ERR_NULL_POINTER;
+  tmw::QuantParams p{};
+  p.x = input;
+  p.ldx = input_row_stride;
+  p.q = out;
+  p.static_scale = scale;
+  p.rows = rows;
+  p.cols = cols;
+  return tmw::launch_quant<tmw::kStatic>(p, input_dtype, tmw::as_stream(stream));
+}
+
+int tm_quantize_weight_int8(int8_t* q, float* scales, const void* w, int w_dtype, int64_t n,
+                            int64_t k, void* stream) {
+  if (int s = tmw::check_rows_cols(n, k, k)) return s;
+  if (n == 0) return TM_OK;
+  if (!q || !scales || !w) return TM_ERR_NULL_POINTER;
+  tmw::QuantParams p{};
+  p.x = w;
+  p.ldx = k;
+  p.q = q;
+  p.scales = scales;
+  p.rows = n;
+  p.cols = k;
+  return tmw::launch_quant<tmw::kWeight>(p, w_dtype, tmw::as_stream(stream));
+}
+
+int tm_modulate_int8_quant(int8_t* out, float* scales, void* hidden_out, const void* x,
+                           const void* shift, const void* scale, const int64_t* index,
+                           int64_t table_stride, int64_t rows, int64_t cols, void* stream) {
+  if (int s = tmw::check_rows_cols(rows, cols, cols)) return s;
+  if (table_stride < cols) return TM_ERR_SHAPE;
+  if (rows == 0) return TM_OK;
+  if (!out || !scales || !x || !shift || !scale) return TM_ERR_NULL_POINTER;
+  tmw::QuantParams p{};
+  p.x = x;
+  p.ldx = cols;
+  p.q = out;
+  p.scales = scales;
+  p.hidden_out = static_cast<__nv_bfloat16*>(hidden_out);
+  p.shift = static_cast<const __nv_bfloat16*>(shift);
+  p.mod_scale = static_cast<const __nv_bfloat16*>(scale);
+  p.index = index;
+  p.table_stride = table_stride;
+  p.rows = rows;
+  p.cols = cols;
+  return tmw::launch_modulate<tmw::kModulate>(p, tmw::as_stream(stream));
+}
+
+int tm_rms_norm_modulate_int8_quant(int8_t* out, float* scales, void* hidden_out,
+                                    const void* x, const void* norm_weight, float eps,
+                                    const void* shift, const void* scale, const int64_t* index,
+                                    int64_t table_stride, int64_t rows, int64_t cols,
+                                    void* stream) {
+  if (int s = tmw::check_rows_cols(rows, cols, cols)) return s;
+  if (table_stride < cols) return TM_ERR_SHAPE;
+  if (rows == 0) return TM_OK;
+  if (!out || !scales || !x || !norm_weight || !shift || !scale) return TM_ERR_NULL_POINTER;
+  tmw::QuantParams p{};
+  p.x = x;
+  p.ldx = cols;
+  p.q = out;
+  p.scales = scales;
+  p.hidden_out = static_cast<__nv_bfloat16*>(hidden_out);
+  p.shift = static_cast<const __nv_bfloat16*>(shift);
+  p.mod_scale = static_cast<const __nv_bfloat16*>(scale);
+  p.index = index;
+  p.table_stride = table_stride;
+  p.norm_w = static_cast<const __nv_bfloat16*>(norm_weight);
+  p.eps = eps;
+  p.rows = rows;
+  p.cols = cols;
+  return tmw::launch_modulate<tmw::kRmsModulate>(p, tmw::as_stream(stream));
+}
+
+}  // extern "C"

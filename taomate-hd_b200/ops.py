@@ -1,0 +1,171 @@
+"""Drop-in replacement for the ``vllm._custom_ops`` functions the reference uses.
+
+The reference loads ``vllm._custom_ops`` (src/taomate_hd/inference/w8a8.py:76-86)
+and calls ``scaled_int8_quant`` and ``cutlass_scaled_mm``
+(src/taomate_hd/inference/w8a8.py:141-144); its workspace calls the
+out-variant operators ``torch.ops._C.dynamic_scaled_int8_quant`` and
+``torch.ops._C.cutlass_scaled_mm`` (w8a8.py:22-35, :71-72).  This module
+exposes the same two functions with the same signatures, return values and
+error behaviour, backed by ``torch.ops.taomate_w8a8`` (hand-written sm_100a
+kernels), plus the fused variants this package adds.  Every function
+requires CUDA tensors: there is no CPU path.
+"""
+from __future__ import annotations
+
+import torch
+
+from ._native import load_torch_ops
+
+load_torch_ops()
+_ops = torch.ops.taomate_w8a8
+
+EPI_GELU_TANH = 0x1
+
+
+def _require_cuda(*tensors: torch.Tensor | None) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("taomate_hd_b200 ops require CUDA tensors (there is no CPU path)")
+
+
+def scaled_int8_quant(
+    input: torch.Tensor,
+    scale: torch.Tensor | None = None,
+    azp: torch.Tensor | None = None,
+    symmetric: bool = True,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor | None]:
+    """Quantise ``input`` to int8; returns ``(int8, scales, None)``.
+
+    ``scale is None``: dynamic per-token symmetric quantisation, scales shaped
+    ``[numel // input.shape[-1], 1]`` (vLLM ``scaled_int8_quant``, the call at
+    w8a8.py:141).  Otherwise static per-tensor quantisation with ``scale``.
+    Asymmetric quantisation (``azp`` / ``symmetric=False``) is not used by the
+    reference and raises.
+    """
+    _require_cuda(input, scale)
+    if azp is not None or not symmetric:
+        raise NotImplementedError("asymmetric int8 quantisation is not supported")
+    output = torch.empty_like(input, dtype=torch.int8)
+    if scale is not None:
+        _ops.static_scaled_int8_quant(output, input, scale, None)
+        return output, scale, None
+    input_scales = torch.empty(
+        (input.numel() // input.shape[-1], 1), device=input.device, dtype=torch.float32
+    )
+    _ops.dynamic_scaled_int8_quant(output, input.contiguous(), input_scales, None)
+    return output, input_scales, None
+
+
+def cutlass_scaled_mm(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    scale_a: torch.Tensor,
+    scale_b: torch.Tensor,
+    out_dtype: torch.dtype,
+    bias: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """``out = (scale_a * a) @ (scale_b * b)`` in ``out_dtype`` (+ bias).
+
+    ``a``: int8 ``[..., K]``; ``b``: int8 ``[K, N]`` column-major (the
+    ``weight.t()`` view of an ``[N, K]`` weight); ``scale_a`` per-tensor or
+    per-token fp32; ``scale_b`` per-tensor or per-channel fp32 (w8a8.py:142-144).
+    Requires K and N to be multiples of 16 (vLLM's CUTLASS contract); vLLM's
+    Triton fallback for other shapes is not provided.
+    """
+    _require_cuda(a, b, scale_a, scale_b, bias)
+    if out_dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError("out_dtype must be torch.bfloat16 or torch.float16")
+    if bias is not None and (bias.numel() != b.shape[1] or bias.dtype != out_dtype):
+        raise ValueError("bias must have b.shape[1] elements of out_dtype")
+    if b.shape[0] % 16 or b.shape[1] % 16:
+        raise ValueError("cutlass_scaled_mm requires K and N to be multiples of 16")
+    target_shape = (*a.shape[:-1], b.shape[1])
+    a2 = a.view(-1, a.shape[-1])
+    out = torch.empty((a2.shape[0], b.shape[1]), dtype=out_dtype, device=a.device)
+    _ops.cutlass_scaled_mm(out, a2, b, scale_a, scale_b, bias)
+    return out.view(*target_shape)
+
+
+def scaled_mm(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    scale_a: torch.Tensor,
+    scale_b: torch.Tensor,
+    out_dtype: torch.dtype = torch.bfloat16,
+    bias: torch.Tensor | None = None,
+    *,
+    gelu_tanh: bool = False,
+    out: torch.Tensor | None = None,
+    acc_debug: torch.Tensor | None = None,
+    tile_n: int = 0,
+) -> torch.Tensor:
+    """:func:`cutlass_scaled_mm` with the fused epilogue options.
+
+    ``gelu_tanh`` applies ``round(gelu_tanh(round(y)))`` to the dequantised
+    (+bias) output; ``acc_debug`` (int32 ``[M, N]``) receives the raw
+    accumulators; ``out`` makes the call allocation-free; ``tile_n`` forces
+    the N-tile width (0 = heuristic).
+    """
+    _require_cuda(a, b, scale_a, scale_b, bias, out, acc_debug)
+    a2 = a.reshape(-1, a.shape[-1])
+    if out is None:
+        out = torch.empty((a2.shape[0], b.shape[1]), dtype=out_dtype, device=a.device)
+    _ops.scaled_mm_i8_ex(out, a2, b, scale_a, scale_b, bias,
+                         EPI_GELU_TANH if gelu_tanh else 0, acc_debug, tile_n)
+    return out
+
+
+def quantize_weight_int8(weight: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-output-channel symmetric int8 weight conversion on the GPU.
+
+    Bit-exact with ``_quantize_cutlass_w8a8_weight`` (w8a8.py:175-179);
+    returns ``(int8 [N, K], fp32 scales [N, 1])``.
+    """
+    _require_cuda(weight)
+    w = weight.contiguous()
+    q = torch.empty_like(w, dtype=torch.int8)
+    scales = torch.empty((w.shape[0], 1), device=w.device, dtype=torch.float32)
+    _ops.quantize_weight_int8(q, scales, w)
+    return q, scales
+
+
+def modulate_int8_quant(
+    x: torch.Tensor,
+    shift: torch.Tensor,
+    scale: torch.Tensor,
+    index: torch.Tensor | None = None,
+    *,
+    return_hidden: bool = False,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor | None]:
+    """adaLN modulate (fused_kernels.py:220-236) fused into the per-token quant.
+
+    Returns ``(int8 like x, fp32 scales [rows, 1], hidden or None)`` where
+    hidden is the bf16 modulated activation.
+    """
+    _require_cuda(x, shift, scale, index)
+    rows = x.numel() // x.shape[-1]
+    q = torch.empty_like(x, dtype=torch.int8)
+    s = torch.empty((rows, 1), device=x.device, dtype=torch.float32)
+    hidden = torch.empty_like(x) if return_hidden else None
+    _ops.modulate_int8_quant(q, s, hidden, x, shift, scale, index)
+    return q, s, hidden
+
+
+def rms_norm_modulate_int8_quant(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    eps: float,
+    shift: torch.Tensor,
+    scale: torch.Tensor,
+    index: torch.Tensor | None = None,
+    *,
+    return_hidden: bool = False,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor | None]:
+    """RMSNorm + adaLN modulate (fused_kernels.py:322-347) fused into the quant."""
+    _require_cuda(x, weight, shift, scale, index)
+    rows = x.numel() // x.shape[-1]
+    q = torch.empty_like(x, dtype=torch.int8)
+    s = torch.empty((rows, 1), device=x.device, dtype=torch.float32)
+    hidden = torch.empty_like(x) if return_hidden else None
+    _ops.rms_norm_modulate_int8_quant(q, s, hidden, x, weight, float(eps), shift, scale, index)
+    return q, s, hidden
