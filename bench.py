@@ -1,0 +1,401 @@
+#!/usr/bin/env python
+"""Benchmark of the W8A8 tensor-parallel DiT linear path on B200.
+
+Workload (the 480p LOW-stage DiT MLP): M = 8192
+tokens, d = 3072, ffn = 12288; X bf16 ~N(0,1) with 0.1% outlier channels x20;
+weights N(0,0.02) quantised per output channel; one step =
+quant(X) -> fc1 (column-parallel, +bias, GELU-tanh fused) -> quant ->
+fc2 (row-parallel, +bias) -> reduce-scatter of the fc2 partials over the TP
+group.  The TP degree equals the GPU count (strong scaling: the total work
+is fixed).  Metric: whole-job int8 TOPS = 2 * (2 M d ffn) / step time.
+
+Timing: W untimed warm-up steps; K timed steps, each bracketed by CUDA events
+on the launching stream, with a 256 MiB buffer written between steps to
+flush L2 (outside the events); barrier + synchronize around the timed region;
+the max over ranks is reported.  ``e2e`` repeats the step through the same
+public API with the input copied from pinned host memory and the output read
+back each step.
+
+``--impl reference`` times the reference algorithm on the host cores (the
+CPU oracle: per-token quant, exact int32 GEMM, fp32 epilogue), rank 0 only.
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl {ours,reference}]
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "W8A8 TP-linear TOPS & % INT8 peak at 1/2/4/8 B200; ms per 768p DiT block"
+TOKENS, D, FFN = 8192, 3072, 12288
+BLOCK_TOKENS, HEADS, HEAD_DIM = 20480, 24, 128
+FLUSH_BYTES = 256 * 1024 * 1024
+WORKLOAD = "480p LOW-stage DiT MLP (BASELINE configs[1]): fc1 column-parallel +bias+GELU-tanh, fc2 row-parallel + reduce-scatter"
+
+
+def parse_args(argv=None):
+    p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-extras", action="store_true")
+    args = p.parse_args(argv)
+    if args.warmup < 3:
+        p.error("--warmup must be at least 3")
+    if args.steps < 1:
+        p.error("--steps must be positive")
+    return args
+
+
+# ----------------------------------------------------------------- peaks
+def load_peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return {"hbm_gbs": float(data["hbm_gbs"]), "bf16_tflops": float(data["bf16_tflops"]),
+                "bf16_tflops_sustained": float(data.get("bf16_tflops_sustained", data["bf16_tflops"])),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+def ncu_traffic_per_launch(profile: str) -> float | None:
+    """DRAM bytes per launch recorded in a committed ncu summary, if present."""
+    path = ROOT / "profiles" / profile
+    if not path.exists():
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", path.read_text())
+    return float(m.group(1)) if m else None
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling (200 ms) of SM clocks and throttle reasons."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        time.sleep(0.25)
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        self.file.flush()
+        rows = []
+        for line in Path(self.file.name).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                try:
+                    rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+                except ValueError:
+                    continue
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, flags in rows for i, f in enumerate(flags)
+                          if f.lower().startswith("active")})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ----------------------------------------------------------------- distributed
+def setup_distributed(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    if world == 1 and args.gpus > 1:
+        raise SystemExit("--gpus N > 1 must be launched with torch.distributed.run (one rank per GPU)")
+    return world, rank, local
+
+
+def max_over_ranks(value: float, world: int, device) -> float:
+    if world == 1:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int) -> None:
+    if world > 1:
+        torch.distributed.barrier()
+
+
+# ----------------------------------------------------------------- CPU reference
+def cpu_reference_setup(rows: int, seed: int = 0):
+    """Oracle operands for ``rows`` tokens of the workload at TP=1."""
+    from oracle import w8a8_oracle as orc
+
+    x = orc.activation(rows, D, seed)
+    w1q, w1s = orc.quantize_weight(orc.weight(FFN, D, seed + 10))
+    w2q, w2s = orc.quantize_weight(orc.weight(D, FFN, seed + 20))
+    g = torch.Generator().manual_seed(seed + 1)
+    b1 = (torch.randn(FFN, generator=g) * 0.01).to(torch.bfloat16)
+    b2 = (torch.randn(D, generator=g) * 0.01).to(torch.bfloat16)
+    return x, (w1q, w1s, b1), (w2q, w2s, b2)
+
+
+def cpu_reference_step(x, fc1, fc2):
+    from oracle import w8a8_oracle as orc
+
+    q1, s1 = orc.dynamic_scaled_int8_quant(x)
+    h, _ = orc.scaled_mm(q1, fc1[0], s1, fc1[1], fc1[2], torch.bfloat16, gelu=True)
+    q2, s2 = orc.dynamic_scaled_int8_quant(h)
+    y, _ = orc.scaled_mm(q2, fc2[0], s2, fc2[1], fc2[2], torch.bfloat16)
+    return y
+
+
+def time_cpu_reference(rows: int, min_seconds: float, max_passes: int) -> dict:
+    torch.set_num_threads(os.cpu_count() or 1)
+    x, fc1, fc2 = cpu_reference_setup(rows)
+    cpu_reference_step(x, fc1, fc2)  # warm-up
+    times = []
+    t_end = time.perf_counter() + min_seconds
+    while len(times) < max_passes and (not times or time.perf_counter() < t_end):
+        t0 = time.perf_counter()
+        cpu_reference_step(x, fc1, fc2)
+        times.append(time.perf_counter() - t0)
+    ops = 2 * 2 * rows * D * FFN
+    per = statistics.mean(times)
+    return {"value": ops / per / 1e12, "unit": "TOPS", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{rows} of {TOKENS} tokens at TP=1, {len(times)} passes of {per * 1e3:.1f} ms "
+                      "(oracle quant + torch._int_mm + fp32 epilogue), TOPS of the sample"}
+
+
+def run_reference(args) -> int:
+    world, rank, _ = setup_distributed(args)
+    if rank != 0:
+        return 0
+    torch.set_num_threads(os.cpu_count() or 1)
+    rows = 128
+    x, fc1, fc2 = cpu_reference_setup(rows)
+    for _ in range(args.warmup):
+        cpu_reference_step(x, fc1, fc2)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_reference_step(x, fc1, fc2)
+    per = (time.perf_counter() - t0) / args.steps
+    ops = 2 * 2 * rows * D * FFN
+    value = ops / per / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic",
+        "config": {"workload": WORKLOAD, "tokens": TOKENS, "d": D, "ffn": FFN,
+                   "parallelism": f"tp{args.gpus}", "sample_tokens": rows},
+        "cpu_baseline": {"value": value, "unit": "TOPS", "cores": torch.get_num_threads(),
+                         "kind": "port",
+                         "sample": f"{rows} of {TOKENS} tokens per step at TP=1 on the host cores "
+                                   "(the reference's arithmetic restated in oracle/; the reference's "
+                                   "own int8 GEMM (vLLM cutlass_scaled_mm) has no CPU path and "
+                                   "refuses int8 on sm_100)"},
+        "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ----------------------------------------------------------------- our arm
+def run_ours(args) -> int:
+    world, rank, local = setup_distributed(args)
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        torch.distributed.init_process_group(
+            "nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    from taomate_hd_b200.dit import TPW8A8BlockChain, TPW8A8MLP
+    from taomate_hd_b200.parallel import ParallelContext
+
+    ctx = ParallelContext(tp_world_size=world, tp_rank=rank,
+                          tp_group=torch.distributed.group.WORLD if world > 1 else None)
+    mlp = TPW8A8MLP(TOKENS, D, FFN, ctx, device, seed=0)
+    g = torch.Generator(device=device).manual_seed(1234)
+    x = torch.randn(TOKENS, D, generator=g, device=device)
+    outliers = torch.randperm(D, generator=g, device=device)[: max(1, D // 1000)]
+    x[:, outliers] *= 20
+    x = x.to(torch.bfloat16)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=device)
+
+    for _ in range(args.warmup):
+        mlp.forward(x)
+        flush.zero_()
+    torch.cuda.synchronize()
+    barrier(world)
+
+    K = args.steps
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    gemm_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(K)]
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        barrier(world)
+        wall0 = time.perf_counter()
+        for i in range(K):
+            flush.zero_()
+            starts[i].record()
+            mlp.forward(x, gemm_ev[i])
+            ends[i].record()
+        torch.cuda.synchronize()
+        barrier(world)
+        wall = time.perf_counter() - wall0
+    clock = clocks.summary()
+    step_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / K
+    gemm_ms = [ev[0].elapsed_time(ev[1]) for ev in gemm_ev] + [ev[2].elapsed_time(ev[3]) for ev in gemm_ev]
+    gemm_avg = sum(gemm_ms) / len(gemm_ms)
+    step_ms = max_over_ranks(step_ms, world, device)
+    gemm_avg = max_over_ranks(gemm_avg, world, device)
+    total_ops = mlp.int8_ops
+    value = total_ops / (step_ms * 1e-3) / 1e12
+
+    # e2e: same step through the public API, input from pinned host memory,
+    # output read back to pinned host memory, inside the timed region.
+    x_host = x.cpu().pin_memory()
+    x_dev = torch.empty_like(x)
+    out_rows = mlp.out.shape[0] if world > 1 else TOKENS
+    y_host = torch.empty(out_rows, D, dtype=torch.bfloat16).pin_memory()
+    for _ in range(args.warmup):
+        x_dev.copy_(x_host, non_blocking=True)
+        y_host.copy_(mlp.forward(x_dev), non_blocking=True)
+    torch.cuda.synchronize()
+    barrier(world)
+    e_s = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    e_e = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    for i in range(K):
+        flush.zero_()
+        e_s[i].record()
+        x_dev.copy_(x_host, non_blocking=True)
+        y_host.copy_(mlp.forward(x_dev), non_blocking=True)
+        e_e[i].record()
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(e_s, e_e)) / K, world, device)
+
+    extras = {}
+    if not args.no_extras:
+        del mlp
+        torch.cuda.empty_cache()
+        block = TPW8A8BlockChain(BLOCK_TOKENS, D, HEADS, HEAD_DIM, FFN, ctx, device, seed=7)
+        xb = torch.randn(BLOCK_TOKENS, D, generator=g, device=device).to(torch.bfloat16)
+        for _ in range(3):
+            block.forward(xb)
+        torch.cuda.synchronize()
+        barrier(world)
+        reps = max(5, K // 2)
+        bs = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
+        be = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
+        for i in range(reps):
+            flush.zero_()
+            bs[i].record()
+            block.forward(xb)
+            be[i].record()
+        torch.cuda.synchronize()
+        barrier(world)
+        block_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(bs, be)) / reps, world, device)
+        extras = {"ms_per_768p_block_linear_chain": block_ms,
+                  "block_768p_tops": block.int8_ops / (block_ms * 1e-3) / 1e12,
+                  "block_768p_config": f"M={BLOCK_TOKENS}, d={D}, QKV N={3 * HEADS * HEAD_DIM}, "
+                                       f"out-proj, fc1 N={FFN} (+GELU), fc2; all-reduce after "
+                                       f"row-parallel linears; no LoRA / modulate fusion"}
+
+    if rank == 0:
+        peaks = load_peaks()
+        peak_int8 = 2.0 * peaks["bf16_tflops"]
+        per_launch_ops = 2 * TOKENS * D * (FFN // world)
+        achieved = per_launch_ops / (gemm_avg * 1e-3) / 1e12
+        traffic = ncu_traffic_per_launch("gemm_i8_mlp480p_fc1.md") if world == 1 else None
+        cpu_base = None
+        if world == 1 and not args.no_cpu_baseline:
+            cpu_base = time_cpu_reference(rows=512, min_seconds=10.0, max_passes=40)
+        line = {
+            "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world, "steps": K,
+            "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "tokens": TOKENS, "d": D, "ffn": FFN,
+                       "parallelism": f"tp{world}", "reduce": "nccl reduce_scatter_tensor",
+                       "l2": "flushed between steps (256 MiB write outside the step events)"},
+            "pct_int8_peak": 100.0 * value / peak_int8,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_int8,
+                         "unit": "TOPS", "frac": achieved / peak_int8, "traffic": traffic,
+                         "kernel": "gemm_i8_kernel<256,4,bf16> (fc1/fc2 launches)",
+                         "peak_source": f"2 x {peaks['source']} bf16 dense "
+                                        f"({peaks['bf16_tflops']:.0f} TFLOP/s, MEASURED_PEAKS.json): "
+                                        "sm_100 int8 tensor rate is twice bf16",
+                         "frac_of_sustained": achieved / (2.0 * peaks["bf16_tflops_sustained"])},
+            "clocks": clock,
+            "e2e": {"value": total_ops / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS",
+                    "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": world * x.numel() * x.element_size(),
+                    "d2h_bytes_per_step": world * y_host.numel() * y_host.element_size()},
+            "gpu_launches": K * mlp_launches(),
+            "wall_s_timed_region": wall,
+            "extras": extras,
+        }
+        if cpu_base is not None:
+            line["cpu_baseline"] = cpu_base
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+def mlp_launches() -> int:
+    from taomate_hd_b200.dit import TPW8A8MLP
+
+    return TPW8A8MLP.launches_per_step
+
+
+def main(argv=None) -> int:
+    args = parse_args(argv)
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

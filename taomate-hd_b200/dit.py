@@ -1,0 +1,215 @@
+"""W8A8 tensor-parallel DiT linear stages on preallocated buffers.
+
+These are the shapes of the BASELINE configurations, built from the
+package's operators (no reference counterpart as a class: the reference runs
+the same linears inside its DiT block, model/layers.py:346-368, :502-523):
+
+* ``TPW8A8MLP``        fc1 column-parallel (+bias, GELU-tanh in the GEMM
+                       epilogue) -> per-token quant over the local K ->
+                       fc2 row-parallel, partials summed by a row reduce-scatter
+                       (or all-reduce).  The fc2 bias is added once, by TP rank 0
+                       inside its GEMM epilogue, which makes the sum equal to
+                       ``reduce(partial) + bias`` (linear.py:284-289).
+* ``TPW8A8AttnProj``   merged QKV column-parallel (each of Q, K, V sharded
+                       separately, linear.py:207-215) and the row-parallel
+                       out-projection with an all-reduce.
+* ``TPW8A8BlockChain`` QKV, out-proj, fc1, fc2 of one block in sequence.
+
+Every ``forward`` writes into buffers allocated at construction, so a step
+allocates nothing and can be captured in a CUDA graph.  Weights are random
+(``N(0, 0.02)``) and quantised per output channel on the GPU; row-parallel
+weights are quantised after K-sharding, as the reference does.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import ops
+from .collectives import all_reduce_sum_inplace_, reduce_scatter_rows
+from .parallel import ParallelContext
+
+
+@dataclass
+class W8Weight:
+    """int8 weight [N, K] with fp32 per-output-channel scales [N] and optional bias [N]."""
+
+    q: torch.Tensor
+    scale: torch.Tensor
+    bias: torch.Tensor | None
+
+    @property
+    def q_t(self) -> torch.Tensor:
+        return self.q.t()
+
+
+def random_bf16(shape: tuple[int, ...], std: float, seed: int, device: torch.device) -> torch.Tensor:
+    g = torch.Generator(device=device).manual_seed(seed)
+    return (torch.randn(shape, generator=g, device=device, dtype=torch.float32) * std).to(torch.bfloat16)
+
+
+def column_weight(
+    n: int, k: int, ctx: ParallelContext, seed: int, device: torch.device, *,
+    bias: bool, output_sizes: tuple[int, ...] | None = None,
+) -> W8Weight:
+    """Column-parallel shard of a random [n, k] weight (per-projection for merged)."""
+    full = random_bf16((n, k), 0.02, seed, device)
+    t, r = ctx.tp_world_size, ctx.tp_rank
+    sizes = output_sizes or (n,)
+    pieces, offset = [], 0
+    for size in sizes:
+        local = size // t
+        pieces.append(full.narrow(0, offset + r * local, local))
+        offset += size
+    local_w = torch.cat(pieces, 0).contiguous()
+    q, s = ops.quantize_weight_int8(local_w)
+    b = None
+    if bias:
+        full_b = random_bf16((n,), 0.01, seed + 1, device)
+        pieces, offset = [], 0
+        for size in sizes:
+            local = size // t
+            pieces.append(full_b.narrow(0, offset + r * local, local))
+            offset += size
+        b = torch.cat(pieces, 0).contiguous()
+    return W8Weight(q, s.reshape(-1), b)
+
+
+def row_weight(
+    n: int, k: int, ctx: ParallelContext, seed: int, device: torch.device, *, bias: bool
+) -> W8Weight:
+    """Row-parallel K-shard of a random [n, k] weight, quantised after sharding."""
+    full = random_bf16((n, k), 0.02, seed, device)
+    t, r = ctx.tp_world_size, ctx.tp_rank
+    local_w = full.narrow(1, r * (k // t), k // t).contiguous()
+    q, s = ops.quantize_weight_int8(local_w)
+    b = random_bf16((n,), 0.01, seed + 1, device) if bias else None
+    return W8Weight(q, s.reshape(-1), b)
+
+
+class _Quant:
+    """Preallocated per-token int8 activation buffers."""
+
+    def __init__(self, rows: int, cols: int, device: torch.device):
+        self.q = torch.empty(rows, cols, dtype=torch.int8, device=device)
+        self.s = torch.empty(rows, 1, dtype=torch.float32, device=device)
+
+    def __call__(self, x: torch.Tensor) -> None:
+        torch.ops.taomate_w8a8.dynamic_scaled_int8_quant(self.q, x, self.s, None)
+
+
+def _gemm(q: _Quant, w: W8Weight, out: torch.Tensor, *, bias: torch.Tensor | None,
+          gelu: bool = False) -> torch.Tensor:
+    torch.ops.taomate_w8a8.scaled_mm_i8_ex(out, q.q, w.q_t, q.s, w.scale, bias,
+                                           ops.EPI_GELU_TANH if gelu else 0, None, 0)
+    return out
+
+
+class TPW8A8MLP:
+    """480p LOW-stage MLP, fc1 column + fc2 row (reduce-scatter)."""
+
+    def __init__(self, tokens: int, d: int, ffn: int, ctx: ParallelContext, device: torch.device,
+                 *, seed: int = 0, reduce: str = "reduce_scatter"):
+        t = ctx.tp_world_size
+        if ffn % t or (reduce == "reduce_scatter" and tokens % t):
+            raise ValueError("ffn and tokens must divide by the TP degree")
+        if reduce not in ("reduce_scatter", "all_reduce"):
+            raise ValueError("reduce must be 'reduce_scatter' or 'all_reduce'")
+        self.ctx, self.tokens, self.d, self.ffn, self.reduce = ctx, tokens, d, ffn, reduce
+        self.fc1 = column_weight(ffn, d, ctx, seed + 10, device, bias=True)
+        self.fc2 = row_weight(d, ffn, ctx, seed + 20, device, bias=True)
+        local_ffn = ffn // t
+        self.q1 = _Quant(tokens, d, device)
+        self.h = torch.empty(tokens, local_ffn, dtype=torch.bfloat16, device=device)
+        self.q2 = _Quant(tokens, local_ffn, device)
+        self.partial = torch.empty(tokens, d, dtype=torch.bfloat16, device=device)
+        rows_out = tokens // t if reduce == "reduce_scatter" and t > 1 else tokens
+        self.out = torch.empty(rows_out, d, dtype=torch.bfloat16, device=device)
+
+    @property
+    def int8_ops(self) -> int:
+        """Whole-job int8 GEMM operations of one forward (2 M N K per linear)."""
+        return 2 * 2 * self.tokens * self.d * self.ffn
+
+    # our kernel launches per forward: 2 quant + 2 GEMM
+    launches_per_step = 4
+
+    def forward(self, x: torch.Tensor, gemm_events: list | None = None) -> torch.Tensor:
+        self.q1(x)
+        if gemm_events is not None:
+            gemm_events[0].record()
+        _gemm(self.q1, self.fc1, self.h, bias=self.fc1.bias, gelu=True)
+        if gemm_events is not None:
+            gemm_events[1].record()
+        self.q2(self.h)
+        bias2 = self.fc2.bias if self.ctx.tp_rank == 0 else None
+        if gemm_events is not None:
+            gemm_events[2].record()
+        _gemm(self.q2, self.fc2, self.partial, bias=bias2)
+        if gemm_events is not None:
+            gemm_events[3].record()
+        t = self.ctx.tp_world_size
+        if t == 1:
+            return self.partial
+        if self.reduce == "reduce_scatter":
+            return reduce_scatter_rows(self.partial, group=self.ctx.tp_group, world_size=t,
+                                       out=self.out)
+        return all_reduce_sum_inplace_(self.partial, group=self.ctx.tp_group, world_size=t)
+
+
+class TPW8A8AttnProj:
+    """merged QKV column-parallel + out-proj row-parallel (all-reduce)."""
+
+    def __init__(self, tokens: int, d: int, heads: int, head_dim: int, ctx: ParallelContext,
+                 device: torch.device, *, seed: int = 0):
+        t = ctx.tp_world_size
+        width = heads * head_dim
+        if heads % t:
+            raise ValueError("heads must divide by the TP degree")
+        self.ctx, self.tokens, self.d, self.width = ctx, tokens, d, width
+        self.qkv = column_weight(3 * width, d, ctx, seed + 30, device, bias=True,
+                                 output_sizes=(width, width, width))
+        self.out_proj = row_weight(d, width, ctx, seed + 40, device, bias=True)
+        self.q_in = _Quant(tokens, d, device)
+        self.qkv_out = torch.empty(tokens, 3 * width // t, dtype=torch.bfloat16, device=device)
+        self.q_attn = _Quant(tokens, width // t, device)
+        self.partial = torch.empty(tokens, d, dtype=torch.bfloat16, device=device)
+
+    @property
+    def int8_ops(self) -> int:
+        return 2 * self.tokens * self.d * 3 * self.width + 2 * self.tokens * self.width * self.d
+
+    launches_per_step = 4
+
+    def forward(self, x: torch.Tensor, attn: torch.Tensor | None = None) -> torch.Tensor:
+        """QKV of ``x``; out-proj of ``attn`` (the attention output; defaults to Q's shard)."""
+        self.q_in(x)
+        _gemm(self.q_in, self.qkv, self.qkv_out, bias=self.qkv.bias)
+        a = self.qkv_out[:, : self.width // self.ctx.tp_world_size] if attn is None else attn
+        self.q_attn(a)
+        bias = self.out_proj.bias if self.ctx.tp_rank == 0 else None
+        _gemm(self.q_attn, self.out_proj, self.partial, bias=bias)
+        t = self.ctx.tp_world_size
+        if t == 1:
+            return self.partial
+        return all_reduce_sum_inplace_(self.partial, group=self.ctx.tp_group, world_size=t)
+
+
+class TPW8A8BlockChain:
+    """BASELINE configs[3] linear chain of one DiT block: QKV, out-proj, fc1, fc2."""
+
+    def __init__(self, tokens: int, d: int, heads: int, head_dim: int, ffn: int,
+                 ctx: ParallelContext, device: torch.device, *, seed: int = 0):
+        self.attn = TPW8A8AttnProj(tokens, d, heads, head_dim, ctx, device, seed=seed)
+        self.mlp = TPW8A8MLP(tokens, d, ffn, ctx, device, seed=seed + 100, reduce="all_reduce")
+
+    @property
+    def int8_ops(self) -> int:
+        return self.attn.int8_ops + self.mlp.int8_ops
+
+    launches_per_step = 8
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        h = self.attn.forward(x)
+        return self.mlp.forward(h)

@@ -101,11 +101,31 @@ def main(outdir: str) -> int:
         quant[f"{name}.q"] = q.cpu().numpy()
         quant[f"{name}.s"] = s.cpu().numpy().reshape(-1)
     np.savez_compressed(root / "vllm_quant.npz", meta=np.array(json.dumps(meta)), **quant)
+    # vLLM's CUTLASS int8 kernels refuse sm_100 ("Int8 not supported on
+    # SM100"); the scaled-GEMM vectors then come from vLLM's own Triton
+    # implementation of the same operator (its fallback for other shapes).
+    mm_impl = "cutlass_scaled_mm"
+    scaled_mm = ops.cutlass_scaled_mm
+    try:
+        c0 = mm_cases()[0]
+        scaled_mm(c0["a"].cuda(), c0["b"].cuda().t(), c0["sa"].cuda(), c0["sb"].cuda(),
+                  c0["dtype"])
+    except RuntimeError as exc:
+        from vllm.model_executor.layers.quantization.compressed_tensors.triton_scaled_mm import (
+            triton_scaled_mm,
+        )
+
+        mm_impl = f"triton_scaled_mm (cutlass_scaled_mm raised: {str(exc).splitlines()[0][:160]})"
+
+        def scaled_mm(a, b, sa, sb, dtype, bias=None):
+            # the Triton entry point takes per-channel scales as [N, 1]
+            return triton_scaled_mm(a, b, sa, sb.reshape(-1, 1), dtype, bias)
+    meta["scaled_mm_impl"] = mm_impl
     mm = {}
     for i, c in enumerate(mm_cases()):
         a, b = c["a"].cuda(), c["b"].cuda()
         bias = c["bias"].cuda() if c["bias"] is not None else None
-        y = ops.cutlass_scaled_mm(a, b.t(), c["sa"].cuda(), c["sb"].cuda(), c["dtype"], bias)
+        y = scaled_mm(a, b.t(), c["sa"].cuda(), c["sb"].cuda(), c["dtype"], bias)
         mm[f"{i}.a"] = c["a"].numpy()
         mm[f"{i}.b"] = c["b"].numpy()
         mm[f"{i}.sa"] = c["sa"].numpy().reshape(-1)

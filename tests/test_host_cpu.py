@@ -1,0 +1,235 @@
+"""CPU: host-side logic of the package against the reference's own outputs,
+plus the C-ABI library's exports and host-side argument checks."""
+from __future__ import annotations
+
+import ctypes
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from taomate_hd_b200 import build as native_build
+from taomate_hd_b200 import capi as capi_mod
+from taomate_hd_b200 import lora, w8a8
+from taomate_hd_b200.linear import ColumnParallelLinear, MergedColumnParallelLinear, RowParallelLinear
+from taomate_hd_b200.parallel import ParallelContext, current_parallel_context, use_parallel_context
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def _bf16(bits: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(bits.view(np.int16).copy()).view(torch.bfloat16)
+
+
+@pytest.fixture(scope="module")
+def ref():
+    return np.load(GOLDEN / "reference_host.npz"), json.loads((GOLDEN / "reference_host.json").read_text())
+
+
+# ------------------------------------------------------------------ policy
+def test_policy_matches_reference(ref):
+    _, meta = ref
+    mine = w8a8.resolve_h3_cutlass_w8a8_policy(
+        meta["policy_input_names"], policy=w8a8.INTERIOR_FC1_QKV_CUTLASS_W8A8_POLICY)
+    assert mine == meta["policy"]
+    rev = w8a8.resolve_h3_cutlass_w8a8_policy(
+        meta["policy_input_names"][::-1], policy=w8a8.INTERIOR_FC1_QKV_CUTLASS_W8A8_POLICY)
+    assert rev == meta["policy_reversed_input"]
+
+
+def test_policy_errors_match_reference(ref):
+    _, meta = ref
+    names = meta["policy_input_names"]
+    cases = {"refiner_name": (names + ["token_refiner.blocks.0.attn.qkv_proj"], w8a8.INTERIOR_FC1_QKV_CUTLASS_W8A8_POLICY),
+             "no_candidates": (["final_layer.linear"], w8a8.INTERIOR_FC1_QKV_CUTLASS_W8A8_POLICY),
+             "unknown_policy": (names, "other")}
+    for label, (inp, policy) in cases.items():
+        with pytest.raises(Exception) as info:
+            w8a8.resolve_h3_cutlass_w8a8_policy(inp, policy=policy)
+        assert type(info.value).__name__ == meta["policy_errors"][label]
+
+
+# ------------------------------------------------------------------ sharding
+@pytest.mark.parametrize("tp", [1, 2, 4])
+def test_tp_sharding_matches_reference(ref, tp):
+    arrays, _ = ref
+    full_qkv, full_row = _bf16(arrays["shard.full_qkv"]), _bf16(arrays["shard.full_row"])
+    full_bias = _bf16(arrays["shard.full_bias"])
+    lora_b, lora_a = torch.from_numpy(arrays["shard.lora_b"]), torch.from_numpy(arrays["shard.lora_a"])
+    for rank in range(tp):
+        ctx = ParallelContext(tp_world_size=tp, tp_rank=rank, tp_group=object() if tp > 1 else None)
+        merged = MergedColumnParallelLinear(32, (48, 48, 48), bias=True, gather_output=False,
+                                            dtype=torch.bfloat16, context=ctx, device="meta")
+        col = ColumnParallelLinear(32, 144, bias=True, gather_output=False, dtype=torch.bfloat16,
+                                   context=ctx, device="meta")
+        row = RowParallelLinear(64, 24, bias=False, input_is_parallel=True, dtype=torch.bfloat16,
+                                context=ctx, device="meta")
+        key = f"shard.tp{tp}.r{rank}"
+        assert torch.equal(merged.full_weight_slice(full_qkv), _bf16(arrays[f"{key}.merged_w"]))
+        assert torch.equal(merged.full_bias_slice(full_bias), _bf16(arrays[f"{key}.merged_b"]))
+        assert torch.equal(col.full_weight_slice(full_qkv), _bf16(arrays[f"{key}.column_w"]))
+        assert torch.equal(row.full_weight_slice(full_row), _bf16(arrays[f"{key}.row_w"]))
+        assert torch.equal(lora.column_local_b(lora_b, merged), torch.from_numpy(arrays[f"{key}.lora_b"]))
+        assert torch.equal(lora.row_local_a(lora_a, row), torch.from_numpy(arrays[f"{key}.lora_a"]))
+
+
+def test_shape_errors():
+    with pytest.raises(ValueError):
+        ColumnParallelLinear(8, 10, bias=False, gather_output=False, dtype=torch.bfloat16,
+                             context=ParallelContext(tp_world_size=4, tp_rank=0, tp_group=object()),
+                             device="meta")
+    with pytest.raises(ValueError):
+        MergedColumnParallelLinear(8, (8, 6), bias=False, gather_output=False, dtype=torch.bfloat16,
+                                   context=ParallelContext(tp_world_size=4, tp_rank=0, tp_group=object()),
+                                   device="meta")
+    row = RowParallelLinear(8, 8, bias=False, input_is_parallel=True, dtype=torch.bfloat16, device="meta")
+    with pytest.raises(ValueError):
+        row.full_weight_slice(torch.zeros(8, 9))
+
+
+def test_parallel_context_validation():
+    with pytest.raises(ValueError):
+        ParallelContext(tp_world_size=2, tp_rank=0)          # group required
+    with pytest.raises(ValueError):
+        ParallelContext(tp_world_size=2, tp_rank=2, tp_group=object())
+    ctx = ParallelContext(tp_world_size=2, tp_rank=1, tp_group=object())
+    assert current_parallel_context().tp_world_size == 1
+    with use_parallel_context(ctx):
+        assert current_parallel_context() is ctx
+    assert current_parallel_context().tp_world_size == 1
+    with pytest.raises(TypeError):
+        with use_parallel_context("nope"):
+            pass
+
+
+# ------------------------------------------------------------------ LoRA
+def _lora_module(arrays, which: str, kind: str) -> lora.ParallelLinearLoRA:
+    w = _bf16(arrays[f"lora.{which}_w"])
+    if kind == "column":
+        base = MergedColumnParallelLinear(w.shape[1], (w.shape[0] // 3,) * 3, bias=False,
+                                          gather_output=False, dtype=torch.bfloat16)
+    else:
+        base = RowParallelLinear(w.shape[1], w.shape[0], bias=False, input_is_parallel=True,
+                                 dtype=torch.bfloat16)
+    with torch.no_grad():
+        base.weight.copy_(w)
+    return lora.ParallelLinearLoRA(base, kind=kind, a=_bf16(arrays[f"lora.{which}_a"]),
+                                   b=_bf16(arrays[f"lora.{which}_b"]), scale=float(arrays["lora.scale"]))
+
+
+def test_lora_wrapper_matches_reference(ref):
+    arrays, meta = ref
+    x = _bf16(arrays["lora.x"])
+    with torch.no_grad():
+        y_col = _lora_module(arrays, "qkv", "column")(x)
+        y_row = _lora_module(arrays, "out", "row")(x)
+    assert torch.equal(y_col, _bf16(arrays["lora.qkv_y"]))
+    assert torch.equal(y_row, _bf16(arrays["lora.out_y"]))
+    assert meta["lora_receipt"]["scale"] == float(arrays["lora.scale"])
+
+
+def test_lora_targets_inventory():
+    targets = lora.canonical_h3_lora_targets()
+    assert len(targets) == 208 and targets[0] == "token_refiner.blocks.0.attn.qkv_proj"
+
+
+# ------------------------------------------------------------------ W8A8 adapter
+def test_w8a8_linear_rejects_bias():
+    with pytest.raises(RuntimeError, match="bias-free"):
+        w8a8.cutlass_w8a8_linear(torch, torch.zeros(2, 16), torch.zeros(16, 16, dtype=torch.int8),
+                                 torch.ones(16, 1), bias=torch.zeros(16))
+
+
+def test_weight_conversion_requires_cuda():
+    with pytest.raises(RuntimeError, match="GPU"):
+        w8a8.quantize_cutlass_w8a8_weight(torch, torch.zeros(4, 16, dtype=torch.bfloat16))
+
+
+def test_stream_slot_validation():
+    mod = torch.nn.Module()
+    mod.weight = torch.nn.Parameter(torch.empty(4, 16, dtype=torch.float32), requires_grad=False)
+    with pytest.raises(TypeError):
+        w8a8.prepare_cutlass_w8a8_stream_load_slot_(torch, mod, name="m")
+    mod.weight = torch.nn.Parameter(torch.empty(4, 16, dtype=torch.bfloat16), requires_grad=False)
+    mod.bias = None
+    w8a8.prepare_cutlass_w8a8_stream_load_slot_(torch, mod, name="m")
+    assert mod.weight.dtype == torch.int8 and mod._cutlass_w8a8_stream_load_pending is True
+    with pytest.raises(RuntimeError):
+        w8a8.prepare_cutlass_w8a8_stream_load_slot_(torch, mod, name="m")
+    with pytest.raises(TypeError):
+        w8a8.load_cutlass_w8a8_stream_weight_(torch, mod, torch.zeros(4, 16), name="m")
+    with pytest.raises(ValueError):
+        w8a8.load_cutlass_w8a8_stream_weight_(torch, mod, torch.zeros(4, 8, dtype=torch.bfloat16),
+                                              name="m")
+    with pytest.raises(ValueError):
+        w8a8.load_cutlass_w8a8_stream_weight_(torch, mod, torch.zeros(4, 16, dtype=torch.bfloat16),
+                                              name="m", maximum_temporary_bytes=0)
+
+
+# ------------------------------------------------------------------ native library
+def test_build_is_current():
+    assert native_build.is_current(), "run `python -m taomate_hd_b200.build`"
+
+
+def test_c_abi_exports_every_header_symbol():
+    lib = ctypes.CDLL(str(native_build.CAPI_SO))
+    names = capi_mod.header_symbols()
+    assert len(names) >= 10
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+    assert set(names) == set(capi_mod.SIGNATURES), "ctypes signatures out of sync with the header"
+
+
+def test_c_abi_host_argument_checks():
+    from taomate_hd_b200 import _native
+
+    lib = _native.capi()
+    assert lib.tm_version() >= 100
+    assert capi_mod.status_string(lib, 0) == "ok"
+    p = ctypes.c_void_p(1 << 20)  # never dereferenced: every call below fails validation first
+    quant = lib.tm_dynamic_scaled_int8_quant
+    assert quant(p, p, 0, p, None, 4, 64, 32, None) == capi_mod.TM_ERR_SHAPE       # ld < cols
+    assert quant(p, p, 0, p, None, -1, 64, 64, None) == capi_mod.TM_ERR_SHAPE
+    assert quant(p, p, 7, p, None, 4, 64, 64, None) == capi_mod.TM_ERR_DTYPE
+    assert quant(None, p, 0, p, None, 4, 64, 64, None) == capi_mod.TM_ERR_NULL_POINTER
+    assert quant(p, p, 0, p, p, 4, 64, 64, None) == capi_mod.TM_ERR_UNSUPPORTED     # azp
+    assert quant(p, p, 0, p, None, 0, 64, 64, None) == capi_mod.TM_OK               # no rows
+    mm = lib.tm_cutlass_scaled_mm
+    args = dict(m=128, n=256, k=512)
+    assert mm(p, 0, p, p, p, 128, p, 256, None, 128, 256, 500, 512, 512, 256, None) == capi_mod.TM_ERR_SHAPE
+    assert mm(p, 0, p, p, p, 128, p, 256, None, 128, 250, 512, 512, 512, 256, None) == capi_mod.TM_ERR_SHAPE
+    assert mm(p, 5, p, p, p, 128, p, 256, None, 128, 256, 512, 512, 512, 256, None) == capi_mod.TM_ERR_DTYPE
+    assert mm(p, 0, p, p, p, 7, p, 256, None, 128, 256, 512, 512, 512, 256, None) == capi_mod.TM_ERR_SHAPE
+    assert mm(p, 0, p, p, p, 128, p, 256, None, 128, 256, 512, 520, 512, 256, None) == capi_mod.TM_ERR_ALIGNMENT
+    assert mm(p, 0, p, p, p, 1, p, 256, None, 0, 256, 512, 512, 512, 256, None) == capi_mod.TM_OK
+    assert mm(p, 0, None, p, p, 128, p, 256, None, 128, 256, 512, 512, 512, 256, None) == capi_mod.TM_ERR_NULL_POINTER
+    assert args  # sizes used above
+    tile = lib.tm_scaled_mm_i8_tile
+    assert tile(p, 0, p, p, p, 128, p, 256, None, 128, 256, 512, 512, 512, 256, 0, None, 96, None) == capi_mod.TM_ERR_UNSUPPORTED
+
+
+def test_torch_ops_have_no_cpu_path():
+    from taomate_hd_b200 import ops
+
+    assert hasattr(torch.ops.taomate_w8a8, "cutlass_scaled_mm")
+    with pytest.raises(RuntimeError):
+        ops.scaled_int8_quant(torch.randn(4, 16, dtype=torch.bfloat16))
+    with pytest.raises(NotImplementedError):
+        torch.ops.taomate_w8a8.dynamic_scaled_int8_quant(
+            torch.empty(4, 16, dtype=torch.int8), torch.randn(4, 16, dtype=torch.bfloat16),
+            torch.empty(4, 1), None)
+
+
+def test_stale_build_is_refused(monkeypatch):
+    from taomate_hd_b200 import _native
+
+    monkeypatch.setattr(native_build, "source_digest", lambda: "not-the-stamp")
+    with pytest.raises(_native.NativeLibraryError):
+        _native._require_current()
+
+
+def test_backend_loader_returns_ops_module():
+    backend = w8a8.require_vllm_cutlass_w8a8()
+    assert callable(backend.scaled_int8_quant) and callable(backend.cutlass_scaled_mm)
