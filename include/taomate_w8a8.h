@@ -125,9 +125,11 @@ int tm_scaled_mm_i8_ex(void* out, int out_dtype, const int8_t* a, const int8_t* 
                        int32_t* acc_debug, void* stream);
 
 /*
- * tm_scaled_mm_i8_ex with a forced N-tile width (256, 128 or 64) instead of
- * the size heuristic; lets tests cover every kernel instantiation.  Same
- * reference counterpart as tm_cutlass_scaled_mm.
+ * tm_scaled_mm_i8_ex with a forced tile configuration instead of the size
+ * heuristic; lets tests and benchmarks cover every kernel instantiation.
+ * tile_n: 256, 128, 64 = one-CTA kernel with a 128 x tile_n tile;
+ * 1256, 1192, 1128 = CTA-pair kernel with a 256 x (tile_n - 1000) tile.
+ * Same reference counterpart as tm_cutlass_scaled_mm.
  */
 int tm_scaled_mm_i8_tile(void* out, int out_dtype, const int8_t* a, const int8_t* b,
                          const float* scale_a, int64_t scale_a_numel, const float* scale_b,

@@ -5,27 +5,32 @@
 // Replaces vLLM's cutlass_scaled_mm as called by the reference
 // (src/taomate_hd/inference/w8a8.py:72 and :142-144).
 //
-// Kernel structure (one persistent CTA per SM, 192 threads):
-//   warp 0      TMA producer: per k-block, one 128 x 128 A tile and one
-//               BN x 128 B tile (int8, K-major, 128-byte swizzle) into a
-//               STAGES-deep shared-memory ring; completion by transaction
-//               bytes on the stage's `full` mbarrier.
-//   warp 1      TMEM owner + MMA issuer: allocates 2 x BN TMEM columns (two
-//               int32 accumulators of 128 lanes x BN), one thread issues
-//               tcgen05.mma.kind::i8 (M=128, N=BN, K=32) four times per
-//               k-block and commits to the stage's `empty` barrier; after the
-//               last k-block it commits to the accumulator's `tmem_full`.
-//   warps 2..5  epilogue: wait `tmem_full`, tcgen05.ld 32 columns at a time
-//               (warp w reads TMEM lanes 32*(w%4)..+31 = tile rows), apply
-//               the fp32 dequant / bias / activation, store bf16/fp16, then
-//               release the accumulator via `tmem_empty`.  With two
-//               accumulators the epilogue of tile i overlaps the main loop of
-//               tile i+1.
-// Tiles are visited in groups of 16 M-blocks so that concurrently resident
-// CTAs share A and B panels in L2.  M, N and K tails are handled by TMA
-// zero fill (loads) and predicated stores.
+// Two persistent, warp-specialised kernels share one epilogue:
+//
+//   gemm_i8_pair_kernel  CTA pairs (clusters of 2).  A pair owns a 256 x BN
+//     output tile: each CTA fetches its 128 rows of A and BN/2 rows of B into
+//     its own shared memory; the leader CTA issues tcgen05.mma.cta_group::2
+//     (M=256, N=BN, K=32), which reads both CTAs' operands and writes each
+//     CTA's 128 x BN accumulator into that CTA's TMEM.  Per SM this moves
+//     2/3 of the operand bytes of a 128 x 256 one-CTA tile for the same MMA
+//     work, which is what lets the tensor pipe run near its rate from L2.
+//   gemm_i8_kernel       one CTA per tile of 128 x BN (small or ragged shapes).
+//
+// Warp roles (320 threads per CTA):
+//   warp 0      TMA producer: a STAGES-deep ring of (A, B) k-blocks of 128
+//               bytes of K, 128-byte swizzled, completion by transaction bytes.
+//   warp 1      TMEM owner (2 x BN int32 columns = two accumulators) and MMA
+//               issuer (one thread; in the pair kernel only on the leader).
+//   warps 2..9  epilogue: warp w reads TMEM lane quarter w % 4 (tile rows
+//               32*(w%4)..+31) and column half (w-2)/4; fp32 dequant
+//               sa * (sb * acc) (+ bias) (+ GELU-tanh) -> bf16/fp16 stores.
+// With two accumulators the epilogue of one tile overlaps the main loop of
+// the next.  Tiles are visited in groups of 16 M-blocks for L2 reuse; tails
+// use TMA zero fill and predicated stores.  Every wait is bounded (ptx.cuh).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+
+#include <cmath>
 
 #include "common.h"
 #include "ptx.cuh"
@@ -33,9 +38,10 @@
 namespace tmw {
 namespace {
 
-constexpr int kBM = 128;
-constexpr int kBK = 128;  // bytes == int8 elements per k-block (one swizzle row)
-constexpr int kThreads = 192;
+constexpr int kBM = 128;  // rows of A per CTA
+constexpr int kBK = 128;  // bytes == int8 elements of K per k-block (one swizzle row)
+constexpr int kThreads = 320;
+constexpr int kEpiWarps = 8;
 constexpr int kGroupM = 16;
 
 struct GemmArgs {
@@ -48,19 +54,9 @@ struct GemmArgs {
   int64_t ldo;
   int32_t* acc_debug;
   int M, N, K;
-  int num_m, num_n, kblocks;
+  int num_m, num_n, kblocks;  // tile grid (in units of the kernel's tile)
   uint32_t epilogue;
   int* status;
-};
-
-template <int BN, int STAGES>
-struct GemmSmem {
-  static constexpr int kABytes = kBM * kBK;
-  static constexpr int kBBytes = BN * kBK;
-  static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kBarOffset = STAGES * kStageBytes;
-  static constexpr int kBarBytes = (2 * STAGES + 4) * 8 + 16;
-  static constexpr int kTotal = kBarOffset + kBarBytes + 1024;  // + alignment slack
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
@@ -77,8 +73,8 @@ __device__ __forceinline__ float gelu_tanh(float x) {
   // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))
   const float k_beta = 0.7978845608028654f;
   const float k_kappa = 0.044715f;
-  const float inner = k_beta * (x + k_kappa * x * x * x);
-  return 0.5f * x * (1.0f + tanhf(inner));
+  const float inner = k_beta * fmaf(k_kappa * x * x, x, x);
+  return 0.5f * x * (1.0f + tanh_approx(inner));
 }
 
 template <typename OutT>
@@ -179,22 +175,82 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& g, const uint32_t* r,
   }
 }
 
+// One epilogue warp's share of a 128 x BN accumulator held in this CTA's
+// TMEM at column `acc_col`: lane quarter warp % 4, column half (warp-2)/4.
+template <int BN, typename OutT>
+__device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tmem_base,
+                                              uint32_t acc_col, int64_t row0, int col0,
+                                              int warp, int lane) {
+  constexpr int kHalf = BN / 2;
+  const int q = warp & 3;
+  const int h = (warp - 2) >> 2;
+  const int64_t row = row0 + q * 32 + lane;
+  const bool row_ok = row < g.M;
+  const float sa = row_ok ? (g.sa_per_row ? __ldg(g.sa + row) : __ldg(g.sa)) : 0.f;
+  const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc_col +
+                         static_cast<uint32_t>(h * kHalf);
+#pragma unroll 1
+  for (int c = 0; c < kHalf / 32; ++c) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c * 32), r);
+    tmem_ld_wait();
+    const int col = col0 + h * kHalf + c * 32;
+    if (row_ok) {
+      if (col < g.N) epilogue16<OutT>(g, r, sa, row, col);
+      if (col + 16 < g.N) epilogue16<OutT>(g, r + 16, sa, row, col + 16);
+    }
+  }
+}
+
+template <int BN_CTA, int STAGES>
+struct Smem {
+  static constexpr int kABytes = kBM * kBK;
+  static constexpr int kBBytes = BN_CTA * kBK;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarOffset = STAGES * kStageBytes;
+  static constexpr int kBarBytes = (2 * STAGES + 4) * 8 + 16;
+  static constexpr int kTotal = kBarOffset + kBarBytes + 1024;  // + alignment slack
+  static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "swizzle atoms need 1 KiB alignment");
+  static_assert(kTotal <= 227 * 1024, "shared memory budget");
+};
+
+struct Barriers {
+  uint64_t* full;
+  uint64_t* empty;
+  uint64_t* tmem_full;
+  uint64_t* tmem_empty;
+  uint32_t* tmem_slot;
+  volatile int* abort_flag;
+};
+
+template <int STAGES>
+__device__ __forceinline__ Barriers carve_barriers(uint8_t* base) {
+  Barriers b;
+  b.full = reinterpret_cast<uint64_t*>(base);
+  b.empty = b.full + STAGES;
+  b.tmem_full = b.empty + STAGES;
+  b.tmem_empty = b.tmem_full + 2;
+  b.tmem_slot = reinterpret_cast<uint32_t*>(b.tmem_empty + 2);
+  b.abort_flag = reinterpret_cast<volatile int*>(b.tmem_slot + 1);
+  return b;
+}
+
+__device__ __forceinline__ uint8_t* align1k(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) &
+                                    ~static_cast<uintptr_t>(1023));
+}
+
+// ====================================================================== one CTA
 template <int BN, int STAGES, typename OutT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                    const GemmArgs g) {
-  using L = GemmSmem<BN, STAGES>;
+  using L = Smem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* smem = align1k(smem_raw);
   uint8_t* s_a = smem;
   uint8_t* s_b = smem + STAGES * L::kABytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
-  uint64_t* empty = full + STAGES;
-  uint64_t* tmem_full = empty + STAGES;
-  uint64_t* tmem_empty = tmem_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + 2);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const Barriers bar = carve_barriers<STAGES>(smem + L::kBarOffset);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -202,14 +258,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&bar.full[s], 1);
+      mbar_init(&bar.empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&tmem_full[b], 1);
-      mbar_init(&tmem_empty[b], 4);
+      mbar_init(&bar.tmem_full[b], 1);
+      mbar_init(&bar.tmem_empty[b], kEpiWarps);
     }
-    *abort_flag = 0;
+    *bar.abort_flag = 0;
     fence_mbarrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -217,34 +273,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tm_b);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 2 * BN);
+    tmem_alloc(bar.tmem_slot, 2 * BN);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t tmem_base = *bar.tmem_slot;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      uint32_t issued_mask = 0;    // stages with a load in flight
-      uint32_t issued_parity = 0;  // parity of that load's full phase
+      uint32_t issued_mask = 0, issued_parity = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
         int mb, nb;
         tile_coords(tile, g.num_m, g.num_n, mb, nb);
         for (int kb = 0; kb < g.kblocks; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, g.status)) {
+          if (!mbar_wait(&bar.empty[stage], phase ^ 1u, bar.abort_flag, g.status)) {
             ok = false;
             break;
           }
-          issued_mask &= ~(1u << stage);  // the previous load on this stage was consumed
-          mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
-          tma_load_2d(&tm_a, &full[stage], s_a + stage * L::kABytes, kb * kBK, mb * kBM);
-          tma_load_2d(&tm_b, &full[stage], s_b + stage * L::kBBytes, kb * kBK, nb * BN);
+          issued_mask &= ~(1u << stage);
+          mbar_arrive_expect_tx(&bar.full[stage], L::kStageBytes);
+          tma_load_2d(&tm_a, &bar.full[stage], s_a + stage * L::kABytes, kb * kBK, mb * kBM);
+          tma_load_2d(&tm_b, &bar.full[stage], s_b + stage * L::kBBytes, kb * kBK, nb * BN);
           issued_mask |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {
@@ -254,31 +308,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (!ok) {
-        // Drain: every copy this thread started must land before exit.
         for (int s = 0; s < STAGES; ++s)
-          if (issued_mask & (1u << s)) mbar_wait_drain(&full[s], (issued_parity >> s) & 1u, g.status);
+          if (issued_mask & (1u << s))
+            mbar_wait_drain(&bar.full[s], (issued_parity >> s) & 1u, g.status);
       }
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t kIdesc = make_idesc_i8(kBM, BN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      bool ok = true;
-      bool issued_any = false;
+      bool ok = true, issued_any = false;
       for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
-        if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1u, abort_flag, g.status)) {
+        if (!mbar_wait(&bar.tmem_empty[acc], acc_phase ^ 1u, bar.abort_flag, g.status)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
         for (int kb = 0; kb < g.kblocks; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, g.status)) {
+          if (!mbar_wait(&bar.full[stage], phase, bar.abort_flag, g.status)) {
             ok = false;
             break;
           }
@@ -286,64 +338,44 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t a_addr = smem_u32(s_a + stage * L::kABytes);
           const uint32_t b_addr = smem_u32(s_b + stage * L::kBBytes);
 #pragma unroll
-          for (int k = 0; k < kBK / 32; ++k) {
+          for (int k = 0; k < kBK / 32; ++k)
             umma_i8(d_tmem, make_desc_kmajor_sw128(a_addr + k * 32),
-                    make_desc_kmajor_sw128(b_addr + k * 32), kIdesc,
-                    (kb | k) != 0 ? 1u : 0u);
-          }
+                    make_desc_kmajor_sw128(b_addr + k * 32), kIdesc, (kb | k) != 0 ? 1u : 0u);
           issued_any = true;
-          umma_commit(&empty[stage]);
+          umma_commit(&bar.empty[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit(&tmem_full[acc]);
+        umma_commit(&bar.tmem_full[acc]);
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1u;
         }
       }
       if (!ok && issued_any) {
-        // Every issued batch of MMAs was followed by a commit to its stage's
-        // `empty` barrier, so the phase of the last such commit completing
-        // means the tensor pipe has drained and TMEM may be released.
+        // Every batch of MMAs was followed by a commit to its stage's `empty`
+        // barrier: once the last one completes the tensor pipe has drained.
         const int last = (stage + STAGES - 1) % STAGES;
-        const uint32_t last_phase = (stage == 0) ? (phase ^ 1u) : phase;
-        mbar_wait_drain(&empty[last], last_phase, g.status);
+        mbar_wait_drain(&bar.empty[last], stage == 0 ? (phase ^ 1u) : phase, g.status);
       }
     }
     __syncwarp();
   } else {
-    // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
       int mb, nb;
       tile_coords(tile, g.num_m, g.num_n, mb, nb);
-      if (!mbar_wait(&tmem_full[acc], acc_phase, abort_flag, g.status)) break;
+      if (!mbar_wait(&bar.tmem_full[acc], acc_phase, bar.abort_flag, g.status)) break;
       tc_fence_after();
-      const int64_t row = static_cast<int64_t>(mb) * kBM + q * 32 + lane;
-      const bool row_ok = row < g.M;
-      const float sa = row_ok ? (g.sa_per_row ? __ldg(g.sa + row) : __ldg(g.sa)) : 0.f;
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                             static_cast<uint32_t>(acc * BN);
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c * 32), r);
-        tmem_ld_wait();
-        const int col0 = nb * BN + c * 32;
-        if (row_ok) {
-          if (col0 < g.N) epilogue16<OutT>(g, r, sa, row, col0);
-          if (col0 + 16 < g.N) epilogue16<OutT>(g, r + 16, sa, row, col0 + 16);
-        }
-      }
+      epilogue_tile<BN, OutT>(g, tmem_base, static_cast<uint32_t>(acc * BN),
+                              static_cast<int64_t>(mb) * kBM, nb * BN, warp, lane);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tmem_empty[acc]);
+      if (lane == 0) mbar_arrive(&bar.tmem_empty[acc]);
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
@@ -359,65 +391,332 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// ------------------------------------------------------------------ host
+// ====================================================================== CTA pair
+// BN is the pair's N tile; each CTA holds BN/2 rows of B and 128 rows of A.
+template <int BN>
+struct PairTmem {
+  static constexpr uint32_t kCols = BN <= 128 ? 256u : 512u;  // power of two >= 2*BN
+};
+
 template <int BN, int STAGES, typename OutT>
-int launch_gemm(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, const GemmArgs& args,
-                cudaStream_t stream) {
-  using L = GemmSmem<BN, STAGES>;
-  static_assert(L::kTotal <= 227 * 1024, "shared memory budget");
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tm_a,
+                        const __grid_constant__ CUtensorMap tm_b, const GemmArgs g) {
+  constexpr int kBNHalf = BN / 2;
+  using L = Smem<kBNHalf, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1k(smem_raw);
+  uint8_t* s_a = smem;
+  uint8_t* s_b = smem + STAGES * L::kABytes;
+  const Barriers bar = carve_barriers<STAGES>(smem + L::kBarOffset);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0 = leader (issues the MMAs)
+  const bool leader = rank == 0;
+  const int tiles = g.num_m * g.num_n;  // pair tiles of 256 x BN
+  const int pair = blockIdx.x >> 1;
+  const int pairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&bar.full[s], 1);
+      mbar_init(&bar.empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bar.tmem_full[b], 1);
+      mbar_init(&bar.tmem_empty[b], 2 * kEpiWarps);  // both CTAs' epilogue warps
+    }
+    *bar.abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_a);
+    tma_prefetch_desc(&tm_b);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(bar.tmem_slot, PairTmem<BN>::kCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *bar.tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_parity = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < tiles; tile += pairs) {
+        int mb, nb;
+        tile_coords(tile, g.num_m, g.num_n, mb, nb);
+        const int a_row = mb * 2 * kBM + static_cast<int>(rank) * kBM;
+        const int b_row = nb * BN + static_cast<int>(rank) * kBNHalf;
+        for (int kb = 0; kb < g.kblocks; ++kb) {
+          if (!mbar_wait(&bar.empty[stage], phase ^ 1u, bar.abort_flag, g.status)) {
+            ok = false;
+            break;
+          }
+          issued_mask &= ~(1u << stage);
+          // The leader's `full` barrier counts the bytes landing in both CTAs.
+          if (leader) mbar_arrive_expect_tx(&bar.full[stage], 2 * L::kStageBytes);
+          const uint32_t full_leader = map_to_cta(smem_u32(&bar.full[stage]), 0);
+          tma_load_2d_pair(&tm_a, full_leader, s_a + stage * L::kABytes, kb * kBK, a_row);
+          tma_load_2d_pair(&tm_b, full_leader, s_b + stage * L::kBBytes, kb * kBK, b_row);
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        if (leader) {
+          for (int s = 0; s < STAGES; ++s)
+            if (issued_mask & (1u << s))
+              mbar_wait_drain(&bar.full[s], (issued_parity >> s) & 1u, g.status);
+        } else {
+          // The peer's copies complete on the leader's barriers, which this
+          // CTA cannot poll; give any in-flight copy ample time to land.
+          const uint64_t t0 = globaltimer_ns();
+          while (globaltimer_ns() - t0 < 2000000ull) __nanosleep(1000);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      constexpr uint32_t kIdesc = make_idesc_i8(2 * kBM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true, issued_any = false;
+      for (int tile = pair; ok && tile < tiles; tile += pairs) {
+        if (!mbar_wait(&bar.tmem_empty[acc], acc_phase ^ 1u, bar.abort_flag, g.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < g.kblocks; ++kb) {
+          if (!mbar_wait(&bar.full[stage], phase, bar.abort_flag, g.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(s_a + stage * L::kABytes);
+          const uint32_t b_addr = smem_u32(s_b + stage * L::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 32; ++k)
+            umma_i8_pair(d_tmem, make_desc_kmajor_sw128(a_addr + k * 32),
+                         make_desc_kmajor_sw128(b_addr + k * 32), kIdesc,
+                         (kb | k) != 0 ? 1u : 0u);
+          issued_any = true;
+          umma_commit_pair(&bar.empty[stage], 0x3);  // frees the stage in both CTAs
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(&bar.tmem_full[acc], 0x3);  // both CTAs' accumulators ready
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (!ok && issued_any) {
+        const int last = (stage + STAGES - 1) % STAGES;
+        mbar_wait_drain(&bar.empty[last], stage == 0 ? (phase ^ 1u) : phase, g.status);
+      }
+    }
+    __syncwarp();
+  } else {
+    const uint32_t empty_leader0 = map_to_cta(smem_u32(&bar.tmem_empty[0]), 0);
+    const uint32_t empty_leader1 = map_to_cta(smem_u32(&bar.tmem_empty[1]), 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = pair; tile < tiles; tile += pairs) {
+      int mb, nb;
+      tile_coords(tile, g.num_m, g.num_n, mb, nb);
+      if (!mbar_wait(&bar.tmem_full[acc], acc_phase, bar.abort_flag, g.status)) break;
+      tc_fence_after();
+      epilogue_tile<BN, OutT>(g, tmem_base, static_cast<uint32_t>(acc * BN),
+                              static_cast<int64_t>(mb) * 2 * kBM + rank * kBM, nb * BN, warp, lane);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc == 0 ? empty_leader0 : empty_leader1);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();  // no CTA leaves while its peer may still signal it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, PairTmem<BN>::kCols);
+  }
+}
+
+// ====================================================================== host
+struct Operands {
+  const int8_t* a;
+  int64_t lda;
+  const int8_t* b;
+  int64_t ldb;
+};
+
+template <int BN, int STAGES, typename OutT>
+int launch_single(const Operands& op, GemmArgs args, int sms, cudaStream_t stream) {
+  using L = Smem<BN, STAGES>;
+  args.num_m = (args.M + kBM - 1) / kBM;
+  args.num_n = (args.N + BN - 1) / BN;
   CUtensorMap ta, tb;
-  if (!encode_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, a, args.K, args.M, lda, kBK, kBM,
-                      CU_TENSOR_MAP_SWIZZLE_128B))
-    return TM_ERR_CUDA;
-  if (!encode_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, b, args.K, args.N, ldb, kBK, BN,
+  if (!encode_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, op.a, args.K, args.M, op.lda, kBK, kBM,
+                      CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, op.b, args.K, args.N, op.ldb, kBK, BN,
                       CU_TENSOR_MAP_SWIZZLE_128B))
     return TM_ERR_CUDA;
   auto kernel = gemm_i8_kernel<BN, STAGES, OutT>;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal) !=
       cudaSuccess)
     return TM_ERR_CUDA;
-  const int dev = current_device();
-  const int sms = sm_count(dev);
-  if (sms <= 0) return TM_ERR_CUDA;
   const int tiles = args.num_m * args.num_n;
-  const int grid = tiles < sms ? tiles : sms;
-  kernel<<<grid, kThreads, L::kTotal, stream>>>(ta, tb, args);
+  kernel<<<tiles < sms ? tiles : sms, kThreads, L::kTotal, stream>>>(ta, tb, args);
   return check_launch();
 }
 
-// Choose the N tile: the one that minimises (waves x per-tile cost), where a
-// tile's main loop costs ~BN and each tile pays a fixed overhead.
-int pick_bn(int num_m, int n, int sms) {
-  int best_bn = 256;
-  long best = -1;
-  for (int bn : {256, 128, 64}) {
-    const long tiles = static_cast<long>(num_m) * ((n + bn - 1) / bn);
-    const long waves = (tiles + sms - 1) / sms;
-    const long cost = waves * (bn + 32);
-    if (best < 0 || cost < best) {
-      best = cost;
-      best_bn = bn;
-    }
-  }
-  return best_bn;
+template <int BN, int STAGES, typename OutT>
+int launch_pair(const Operands& op, GemmArgs args, int max_pairs, cudaStream_t stream) {
+  using L = Smem<BN / 2, STAGES>;
+  args.num_m = (args.M + 2 * kBM - 1) / (2 * kBM);
+  args.num_n = (args.N + BN - 1) / BN;
+  CUtensorMap ta, tb;
+  if (!encode_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, op.a, args.K, args.M, op.lda, kBK, kBM,
+                      CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, op.b, args.K, args.N, op.ldb, kBK,
+                      BN / 2, CU_TENSOR_MAP_SWIZZLE_128B))
+    return TM_ERR_CUDA;
+  auto kernel = gemm_i8_pair_kernel<BN, STAGES, OutT>;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal) !=
+      cudaSuccess)
+    return TM_ERR_CUDA;
+  const int tiles = args.num_m * args.num_n;
+  const int pairs = tiles < max_pairs ? tiles : max_pairs;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = L::kTotal;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kernel, ta, tb, args) != cudaSuccess) return TM_ERR_CUDA;
+  return check_launch();
 }
 
+// Tile configurations: 0 = heuristic; 64/128/256 = one-CTA kernel with that
+// N tile; kPairFlag + {128, 192, 256} = CTA-pair kernel with that N tile.
+constexpr int kPairFlag = 1000;
+
 template <typename OutT>
-int dispatch_gemm(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, GemmArgs args,
-                  int bn, cudaStream_t stream) {
-  args.num_n = (args.N + bn - 1) / bn;
-  switch (bn) {
-    case 256: return launch_gemm<256, 4, OutT>(a, lda, b, ldb, args, stream);
-    case 128: return launch_gemm<128, 6, OutT>(a, lda, b, ldb, args, stream);
-    case 64: return launch_gemm<64, 8, OutT>(a, lda, b, ldb, args, stream);
+int dispatch(const Operands& op, const GemmArgs& args, int cfg, int sms, int max_pairs,
+             cudaStream_t stream) {
+  switch (cfg) {
+    case 256: return launch_single<256, 4, OutT>(op, args, sms, stream);
+    case 128: return launch_single<128, 6, OutT>(op, args, sms, stream);
+    case 64: return launch_single<64, 8, OutT>(op, args, sms, stream);
+    case kPairFlag + 256: return launch_pair<256, 6, OutT>(op, args, max_pairs, stream);
+    case kPairFlag + 192: return launch_pair<192, 7, OutT>(op, args, max_pairs, stream);
+    case kPairFlag + 128: return launch_pair<128, 8, OutT>(op, args, max_pairs, stream);
     default: return TM_ERR_UNSUPPORTED;
   }
+}
+
+// Relative time of a configuration: waves of tiles over the resident CTAs
+// (or pairs) times the per-SM work of one tile (proportional to its N width)
+// divided by that configuration's sustained efficiency.  The efficiencies
+// are B200 measurements at M=20480, N=9216, K=3072 (normalised to the
+// 256-wide pair tile): narrower tiles need more operand bytes per MMA and
+// fall further below the tensor rate.
+double estimate(int cfg, int m, int n, int sms, int max_pairs) {
+  const bool pair = cfg > kPairFlag;
+  const int bn = pair ? cfg - kPairFlag : cfg;
+  double eff;
+  switch (cfg) {
+    case kPairFlag + 256: eff = 1.00; break;
+    case kPairFlag + 192: eff = 0.77; break;
+    case kPairFlag + 128: eff = 0.52; break;
+    case 256: eff = 0.91; break;
+    case 128: eff = 0.60; break;
+    default: eff = 0.30; break;
+  }
+  const double rows = pair ? 2.0 * kBM : kBM;
+  const double tiles = std::ceil(m / rows) * std::ceil(static_cast<double>(n) / bn);
+  const double slots = pair ? max_pairs : sms;
+  const double waves = std::ceil(tiles / slots);
+  return waves * bn / eff;
+}
+
+int pick_config(int m, int n, int sms, int max_pairs) {
+  static const int kConfigs[] = {kPairFlag + 256, kPairFlag + 192, kPairFlag + 128, 256, 128, 64};
+  int best = 256;
+  double best_t = -1.0;
+  for (int cfg : kConfigs) {
+    if (cfg > kPairFlag && max_pairs <= 0) continue;
+    const double t = estimate(cfg, m, n, sms, max_pairs);
+    if (best_t < 0 || t < best_t) {
+      best_t = t;
+      best = cfg;
+    }
+  }
+  return best;
+}
+
+// Resident CTA pairs of the pair kernel on a device (cached per device).
+int max_resident_pairs(int device, int sms) {
+  static int cache[64] = {};
+  if (device < 0 || device >= 64) return 0;
+  if (cache[device] == 0) {
+    using L = Smem<128, 6>;
+    auto kernel = gemm_i8_pair_kernel<256, 6, __nv_bfloat16>;
+    int clusters = 0;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal) ==
+        cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(static_cast<unsigned>(sms & ~1));
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = L::kTotal;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess) clusters = 0;
+    }
+    cudaGetLastError();  // a failed query must not poison later launches
+    cache[device] = clusters > 0 ? clusters : -1;
+  }
+  return cache[device] > 0 ? cache[device] : 0;
 }
 
 int scaled_mm_impl(void* out, int out_dtype, const int8_t* a, const int8_t* b, const float* sa,
                    int64_t sa_numel, const float* sb, int64_t sb_numel, const void* bias,
                    int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldo,
-                   uint32_t epilogue, int32_t* acc_debug, int force_bn, cudaStream_t stream) {
+                   uint32_t epilogue, int32_t* acc_debug, int force_cfg, cudaStream_t stream) {
   if (out_dtype != TM_DTYPE_BF16 && out_dtype != TM_DTYPE_FP16) return TM_ERR_DTYPE;
   if (m < 0 || n <= 0 || k <= 0) return TM_ERR_SHAPE;
   if (m > 0x7fffffffLL || n > 0x7fffffffLL || k > 0x7fffffffLL) return TM_ERR_TOO_LARGE;
@@ -447,15 +746,17 @@ int scaled_mm_impl(void* out, int out_dtype, const int8_t* a, const int8_t* b, c
   args.M = static_cast<int>(m);
   args.N = static_cast<int>(n);
   args.K = static_cast<int>(k);
-  args.num_m = static_cast<int>((m + kBM - 1) / kBM);
   args.kblocks = static_cast<int>((k + kBK - 1) / kBK);
   args.epilogue = epilogue;
   args.status = device_status_ptr(dev);
   if (args.status == nullptr) return TM_ERR_CUDA;
-  const int bn = force_bn ? force_bn : pick_bn(args.num_m, args.N, sms);
+  const int max_pairs = max_resident_pairs(dev, sms);
+  const int cfg = force_cfg ? force_cfg : pick_config(args.M, args.N, sms, max_pairs);
+  if (cfg > kPairFlag && max_pairs <= 0) return TM_ERR_UNSUPPORTED;
+  const Operands op{a, lda, b, ldb};
   if (out_dtype == TM_DTYPE_BF16)
-    return dispatch_gemm<__nv_bfloat16>(a, lda, b, ldb, args, bn, stream);
-  return dispatch_gemm<__half>(a, lda, b, ldb, args, bn, stream);
+    return dispatch<__nv_bfloat16>(op, args, cfg, sms, max_pairs, stream);
+  return dispatch<__half>(op, args, cfg, sms, max_pairs, stream);
 }
 
 }  // namespace
@@ -468,7 +769,7 @@ int tm_cutlass_scaled_mm(void* out, int out_dtype, const int8_t* a, const int8_t
                          int64_t scale_b_numel, const void* bias, int64_t m, int64_t n, int64_t k,
                          int64_t lda, int64_t ldb, int64_t ldo, void* stream) {
   return tmw::scaled_mm_impl(out, out_dtype, a, b, scale_a, scale_a_numel, scale_b, scale_b_numel,
-                            bias, m, n, k, lda, ldb, ldo, 0u, nullptr, 0, tmw::as_stream(stream));
+                             bias, m, n, k, lda, ldb, ldo, 0u, nullptr, 0, tmw::as_stream(stream));
 }
 
 int tm_scaled_mm_i8_ex(void* out, int out_dtype, const int8_t* a, const int8_t* b,
@@ -477,21 +778,29 @@ int tm_scaled_mm_i8_ex(void* out, int out_dtype, const int8_t* a, const int8_t* 
                        int64_t lda, int64_t ldb, int64_t ldo, uint32_t epilogue,
                        int32_t* acc_debug, void* stream) {
   return tmw::scaled_mm_impl(out, out_dtype, a, b, scale_a, scale_a_numel, scale_b, scale_b_numel,
-                            bias, m, n, k, lda, ldb, ldo, epilogue, acc_debug, 0,
-                            tmw::as_stream(stream));
+                             bias, m, n, k, lda, ldb, ldo, epilogue, acc_debug, 0,
+                             tmw::as_stream(stream));
 }
 
-// Same as tm_scaled_mm_i8_ex with a forced N-tile width (256, 128 or 64);
-// used by tests to cover every kernel instantiation.
 int tm_scaled_mm_i8_tile(void* out, int out_dtype, const int8_t* a, const int8_t* b,
                          const float* scale_a, int64_t scale_a_numel, const float* scale_b,
                          int64_t scale_b_numel, const void* bias, int64_t m, int64_t n, int64_t k,
                          int64_t lda, int64_t ldb, int64_t ldo, uint32_t epilogue,
                          int32_t* acc_debug, int tile_n, void* stream) {
-  if (tile_n != 256 && tile_n != 128 && tile_n != 64) return TM_ERR_UNSUPPORTED;
+  switch (tile_n) {
+    case 256:
+    case 128:
+    case 64:
+    case tmw::kPairFlag + 256:
+    case tmw::kPairFlag + 192:
+    case tmw::kPairFlag + 128:
+      break;
+    default:
+      return TM_ERR_UNSUPPORTED;
+  }
   return tmw::scaled_mm_impl(out, out_dtype, a, b, scale_a, scale_a_numel, scale_b, scale_b_numel,
-                            bias, m, n, k, lda, ldb, ldo, epilogue, acc_debug, tile_n,
-                            tmw::as_stream(stream));
+                             bias, m, n, k, lda, ldb, ldo, epilogue, acc_debug, tile_n,
+                             tmw::as_stream(stream));
 }
 
 }  // extern "C"

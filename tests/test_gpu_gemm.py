@@ -44,7 +44,8 @@ def _run(tm_ops, cuda, a, b, sa, sb, bias, out_dtype, gelu=False, tile_n=0):
 @pytest.mark.parametrize(
     "m,n,k",
     [(128, 256, 128), (1, 16, 16), (100, 48, 32), (300, 1008, 208), (257, 512, 3072),
-     (64, 3072, 3072), (1024, 3072, 3072), (513, 1152, 12288)],
+     (64, 3072, 3072), (1024, 3072, 3072), (513, 1152, 12288), (8192, 3072, 1536),
+     (2560, 2304, 3072)],
 )
 def test_scaled_mm_acc_and_output(tm_ops, cuda, m, n, k):
     a, b, sa, sb, _ = _operands(m, n, k, seed=m * 31 + n * 7 + k)
@@ -55,8 +56,9 @@ def test_scaled_mm_acc_and_output(tm_ops, cuda, m, n, k):
     torch.testing.assert_close(out.float(), ref.float(), atol=ATOL, rtol=RTOL)
 
 
-@pytest.mark.parametrize("tile_n", [256, 128, 64])
-@pytest.mark.parametrize("m,n,k", [(200, 400, 256), (129, 272, 640), (384, 1024, 1024)])
+@pytest.mark.parametrize("tile_n", [256, 128, 64, 1256, 1192, 1128])
+@pytest.mark.parametrize("m,n,k", [(200, 400, 256), (129, 272, 640), (384, 1024, 1024),
+                                   (1000, 2112, 384)])
 def test_every_tile_width(tm_ops, cuda, tile_n, m, n, k):
     a, b, sa, sb, bias = _operands(m, n, k, seed=tile_n + m, bias_dtype=torch.bfloat16)
     out, acc = _run(tm_ops, cuda, a, b, sa, sb, bias, torch.bfloat16, tile_n=tile_n)
