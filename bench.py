@@ -347,7 +347,7 @@ def run_ours(args) -> int:
         peak_int8 = 2.0 * peaks["bf16_tflops"]
         per_launch_ops = 2 * TOKENS * D * (FFN // world)
         achieved = per_launch_ops / (gemm_avg * 1e-3) / 1e12
-        traffic = ncu_traffic_per_launch("gemm_i8_mlp480p_fc1.md") if world == 1 else None
+        traffic = ncu_traffic_per_launch("gemm_i8_pair_mlp480p.md") if world == 1 else None
         cpu_base = None
         if world == 1 and not args.no_cpu_baseline:
             cpu_base = time_cpu_reference(rows=512, min_seconds=10.0, max_passes=40)
@@ -361,7 +361,7 @@ def run_ours(args) -> int:
             "pct_int8_peak": 100.0 * value / peak_int8,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_int8,
                          "unit": "TOPS", "frac": achieved / peak_int8, "traffic": traffic,
-                         "kernel": "gemm_i8_kernel<256,4,bf16> (fc1/fc2 launches)",
+                         "kernel": "gemm_i8_pair_kernel<256,6,bf16> (fc1 and fc2 launches)",
                          "peak_source": f"2 x {peaks['source']} bf16 dense "
                                         f"({peaks['bf16_tflops']:.0f} TFLOP/s, MEASURED_PEAKS.json): "
                                         "sm_100 int8 tensor rate is twice bf16",
