@@ -46,6 +46,15 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tm_scaled_mm_i8_ex": (c_int, [*_GEMM, c_u32, c_void_p, c_void_p]),
     "tm_scaled_mm_i8_tile": (c_int, [*_GEMM, c_u32, c_void_p, c_int, c_void_p]),
     "tm_quantize_weight_int8": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_i64, c_i64, c_void_p]),
+    "tm_scaled_mm_i8_reduce_scatter": (
+        c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_void_p, c_i64, c_void_p,
+                c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_void_p, c_void_p, c_int, c_int,
+                c_u32, c_int, c_void_p]),
+    "tm_peer_handle_size": (c_int, []),
+    "tm_peer_alloc": (c_int, [ctypes.c_uint64, ctypes.POINTER(c_void_p), c_void_p]),
+    "tm_peer_open": (c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
+    "tm_peer_close": (c_int, [c_void_p]),
+    "tm_peer_free": (c_int, [c_void_p]),
     "tm_modulate_int8_quant": (
         c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64,
                 c_i64, c_i64, c_void_p]),

@@ -33,6 +33,7 @@
 #include <cmath>
 
 #include "common.h"
+#include "peer_reduce.h"
 #include "ptx.cuh"
 
 namespace tmw {
@@ -57,6 +58,14 @@ struct GemmArgs {
   int num_m, num_n, kblocks;  // tile grid (in units of the kernel's tile)
   uint32_t epilogue;
   int* status;
+  // Row-parallel scatter (fused reduce-scatter); world == 0 disables it.
+  // Rows of owner j (j * rows_per_owner ...) go to peer_recv[j] slot `rank`;
+  // each finished 128-row x tile-width block publishes `epoch` in
+  // peer_flags[j][rank][row block][column tile].
+  int world, rank, rows_per_owner;
+  uint32_t epoch;
+  __nv_bfloat16* peer_recv[kMaxPeers];
+  uint32_t* peer_flags[kMaxPeers];
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
@@ -115,7 +124,7 @@ __device__ __forceinline__ float round_out<__half>(float v) {
 // Epilogue for 16 consecutive columns held in r[0..15] of one row.
 template <typename OutT>
 __device__ __forceinline__ void epilogue16(const GemmArgs& g, const uint32_t* r, float sa,
-                                           int64_t row, int col) {
+                                           OutT* out_row, int32_t* dbg_row, int col) {
   float sb[16];
   if (g.sb_per_col) {
     const float4* p = reinterpret_cast<const float4*>(g.sb + col);
@@ -163,11 +172,11 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& g, const uint32_t* r,
   o1.y = pack2<OutT>(y[10], y[11]);
   o1.z = pack2<OutT>(y[12], y[13]);
   o1.w = pack2<OutT>(y[14], y[15]);
-  uint4* dst = reinterpret_cast<uint4*>(static_cast<OutT*>(g.out) + row * g.ldo + col);
+  uint4* dst = reinterpret_cast<uint4*>(out_row + col);
   dst[0] = o0;
   dst[1] = o1;
-  if (g.acc_debug != nullptr) {
-    uint4* d = reinterpret_cast<uint4*>(g.acc_debug + row * static_cast<int64_t>(g.N) + col);
+  if (dbg_row != nullptr) {
+    uint4* d = reinterpret_cast<uint4*>(dbg_row + col);
     d[0] = make_uint4(r[0], r[1], r[2], r[3]);
     d[1] = make_uint4(r[4], r[5], r[6], r[7]);
     d[2] = make_uint4(r[8], r[9], r[10], r[11]);
@@ -187,6 +196,16 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tmem_b
   const int64_t row = row0 + q * 32 + lane;
   const bool row_ok = row < g.M;
   const float sa = row_ok ? (g.sa_per_row ? __ldg(g.sa + row) : __ldg(g.sa)) : 0.f;
+  OutT* out_row;
+  if (g.world > 0) {
+    const int owner = row_ok ? static_cast<int>(row / g.rows_per_owner) : 0;
+    const int64_t local = row - static_cast<int64_t>(owner) * g.rows_per_owner;
+    out_row = reinterpret_cast<OutT*>(g.peer_recv[owner]) +
+              (static_cast<int64_t>(g.rank) * g.rows_per_owner + local) * g.N;
+  } else {
+    out_row = static_cast<OutT*>(g.out) + row * g.ldo;
+  }
+  int32_t* dbg_row = g.acc_debug != nullptr ? g.acc_debug + row * static_cast<int64_t>(g.N) : nullptr;
   const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc_col +
                          static_cast<uint32_t>(h * kHalf);
 #pragma unroll 1
@@ -196,9 +215,28 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tmem_b
     tmem_ld_wait();
     const int col = col0 + h * kHalf + c * 32;
     if (row_ok) {
-      if (col < g.N) epilogue16<OutT>(g, r, sa, row, col);
-      if (col + 16 < g.N) epilogue16<OutT>(g, r + 16, sa, row, col + 16);
+      if (col < g.N) epilogue16<OutT>(g, r, sa, out_row, dbg_row, col);
+      if (col + 16 < g.N) epilogue16<OutT>(g, r + 16, sa, out_row, dbg_row, col + 16);
     }
+  }
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Scatter mode: after all 8 epilogue warps stored a 128-row block of the
+// tile into its owner's receive slot, publish the block's flag on the owner.
+__device__ __forceinline__ void publish_block(const GemmArgs& g, int64_t row0, int nb, int warp,
+                                              int lane) {
+  __threadfence_system();
+  asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
+  if (warp == 2 && lane == 0) {
+    const int owner = static_cast<int>(row0 / g.rows_per_owner);
+    const int lrb = static_cast<int>((row0 - static_cast<int64_t>(owner) * g.rows_per_owner) / kBM);
+    uint32_t* f = g.peer_flags[owner] +
+                  (static_cast<int64_t>(g.rank) * (g.rows_per_owner / kBM) + lrb) * g.num_n + nb;
+    st_release_sys(f, g.epoch);
   }
 }
 
@@ -373,6 +411,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       epilogue_tile<BN, OutT>(g, tmem_base, static_cast<uint32_t>(acc * BN),
                               static_cast<int64_t>(mb) * kBM, nb * BN, warp, lane);
+      if (g.world > 0 && static_cast<int64_t>(mb) * kBM < g.M)
+        publish_block(g, static_cast<int64_t>(mb) * kBM, nb, warp, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar.tmem_empty[acc]);
@@ -545,8 +585,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tile_coords(tile, g.num_m, g.num_n, mb, nb);
       if (!mbar_wait(&bar.tmem_full[acc], acc_phase, bar.abort_flag, g.status)) break;
       tc_fence_after();
-      epilogue_tile<BN, OutT>(g, tmem_base, static_cast<uint32_t>(acc * BN),
-                              static_cast<int64_t>(mb) * 2 * kBM + rank * kBM, nb * BN, warp, lane);
+      const int64_t row0 = static_cast<int64_t>(mb) * 2 * kBM + rank * kBM;
+      epilogue_tile<BN, OutT>(g, tmem_base, static_cast<uint32_t>(acc * BN), row0, nb * BN, warp,
+                              lane);
+      if (g.world > 0 && row0 < g.M) publish_block(g, row0, nb, warp, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc == 0 ? empty_leader0 : empty_leader1);
@@ -713,10 +755,21 @@ int max_resident_pairs(int device, int sms) {
   return cache[device] > 0 ? cache[device] : 0;
 }
 
+// Fused reduce-scatter request (row-parallel linears); see
+// tm_scaled_mm_i8_reduce_scatter.
+struct ScatterSpec {
+  void* const* peer_recv;
+  void* const* peer_flags;
+  int world;
+  int rank;
+  uint32_t epoch;
+};
+
 int scaled_mm_impl(void* out, int out_dtype, const int8_t* a, const int8_t* b, const float* sa,
                    int64_t sa_numel, const float* sb, int64_t sb_numel, const void* bias,
                    int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldo,
-                   uint32_t epilogue, int32_t* acc_debug, int force_cfg, cudaStream_t stream) {
+                   uint32_t epilogue, int32_t* acc_debug, int force_cfg, cudaStream_t stream,
+                   const ScatterSpec* scatter = nullptr) {
   if (out_dtype != TM_DTYPE_BF16 && out_dtype != TM_DTYPE_FP16) return TM_ERR_DTYPE;
   if (m < 0 || n <= 0 || k <= 0) return TM_ERR_SHAPE;
   if (m > 0x7fffffffLL || n > 0x7fffffffLL || k > 0x7fffffffLL) return TM_ERR_TOO_LARGE;
@@ -726,6 +779,18 @@ int scaled_mm_impl(void* out, int out_dtype, const int8_t* a, const int8_t* b, c
   if (sa_numel != 1 && sa_numel != m) return TM_ERR_SHAPE;
   if (sb_numel != 1 && sb_numel != n) return TM_ERR_SHAPE;
   if (epilogue & ~TM_EPI_GELU_TANH) return TM_ERR_UNSUPPORTED;
+  if (scatter != nullptr) {
+    if (scatter->world < 1 || scatter->world > kMaxPeers) return TM_ERR_TOO_LARGE;
+    if (scatter->rank < 0 || scatter->rank >= scatter->world) return TM_ERR_SHAPE;
+    if (m % (static_cast<int64_t>(scatter->world) * 2 * kBM) != 0) return TM_ERR_SHAPE;
+    if (out_dtype != TM_DTYPE_BF16 || epilogue != 0) return TM_ERR_UNSUPPORTED;
+    if (!scatter->peer_recv || !scatter->peer_flags) return TM_ERR_NULL_POINTER;
+    for (int j = 0; j < scatter->world; ++j) {
+      if (!scatter->peer_recv[j] || !scatter->peer_flags[j]) return TM_ERR_NULL_POINTER;
+      if (!aligned16(scatter->peer_recv[j]) || !aligned16(scatter->peer_flags[j]))
+        return TM_ERR_ALIGNMENT;
+    }
+  }
   if (m == 0) return TM_OK;
   if (!out || !a || !b || !sa || !sb) return TM_ERR_NULL_POINTER;
   if (!aligned16(a) || !aligned16(b) || !aligned16(out) || (bias && !aligned16(bias)) ||
@@ -739,7 +804,7 @@ int scaled_mm_impl(void* out, int out_dtype, const int8_t* a, const int8_t* b, c
   args.sb = sb;
   args.sa_per_row = sa_numel != 1 || m == 1;
   args.sb_per_col = sb_numel != 1 || n == 1;
-  args.bias = bias;
+  args.bias = scatter ? nullptr : bias;  // scatter mode: the owner adds the bias after the sum
   args.out = out;
   args.ldo = ldo;
   args.acc_debug = acc_debug;
@@ -750,13 +815,40 @@ int scaled_mm_impl(void* out, int out_dtype, const int8_t* a, const int8_t* b, c
   args.epilogue = epilogue;
   args.status = device_status_ptr(dev);
   if (args.status == nullptr) return TM_ERR_CUDA;
+  if (scatter != nullptr) {
+    args.world = scatter->world;
+    args.rank = scatter->rank;
+    args.rows_per_owner = static_cast<int>(m / scatter->world);
+    args.epoch = scatter->epoch;
+    for (int j = 0; j < scatter->world; ++j) {
+      args.peer_recv[j] = static_cast<__nv_bfloat16*>(scatter->peer_recv[j]);
+      args.peer_flags[j] = static_cast<uint32_t*>(scatter->peer_flags[j]);
+    }
+  }
   const int max_pairs = max_resident_pairs(dev, sms);
   const int cfg = force_cfg ? force_cfg : pick_config(args.M, args.N, sms, max_pairs);
   if (cfg > kPairFlag && max_pairs <= 0) return TM_ERR_UNSUPPORTED;
   const Operands op{a, lda, b, ldb};
-  if (out_dtype == TM_DTYPE_BF16)
-    return dispatch<__nv_bfloat16>(op, args, cfg, sms, max_pairs, stream);
-  return dispatch<__half>(op, args, cfg, sms, max_pairs, stream);
+  int status = out_dtype == TM_DTYPE_BF16
+                   ? dispatch<__nv_bfloat16>(op, args, cfg, sms, max_pairs, stream)
+                   : dispatch<__half>(op, args, cfg, sms, max_pairs, stream);
+  if (status != TM_OK || scatter == nullptr) return status;
+  // Owner side: wait for every source's blocks, sum in rank order, add bias.
+  const int bn = cfg > kPairFlag ? cfg - kPairFlag : cfg;
+  RsReduceArgs r{};
+  r.recv = static_cast<const __nv_bfloat16*>(scatter->peer_recv[scatter->rank]);
+  r.flags = static_cast<const uint32_t*>(scatter->peer_flags[scatter->rank]);
+  r.bias = static_cast<const __nv_bfloat16*>(bias);
+  r.out = static_cast<__nv_bfloat16*>(out);
+  r.ldo = ldo;
+  r.world = scatter->world;
+  r.rows_per_owner = args.rows_per_owner;
+  r.n = args.N;
+  r.tile_n = bn;
+  r.num_n = (args.N + bn - 1) / bn;
+  r.epoch = scatter->epoch;
+  r.status = args.status;
+  return launch_rs_reduce(r, stream);
 }
 
 }  // namespace
@@ -780,6 +872,18 @@ int tm_scaled_mm_i8_ex(void* out, int out_dtype, const int8_t* a, const int8_t* 
   return tmw::scaled_mm_impl(out, out_dtype, a, b, scale_a, scale_a_numel, scale_b, scale_b_numel,
                              bias, m, n, k, lda, ldb, ldo, epilogue, acc_debug, 0,
                              tmw::as_stream(stream));
+}
+
+int tm_scaled_mm_i8_reduce_scatter(void* out, const int8_t* a, const int8_t* b,
+                                   const float* scale_a, int64_t scale_a_numel,
+                                   const float* scale_b, int64_t scale_b_numel, const void* bias,
+                                   int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
+                                   int64_t ldo, void* const* peer_recv, void* const* peer_flags,
+                                   int world, int rank, uint32_t epoch, int tile_n, void* stream) {
+  const tmw::ScatterSpec spec{peer_recv, peer_flags, world, rank, epoch};
+  return tmw::scaled_mm_impl(out, TM_DTYPE_BF16, a, b, scale_a, scale_a_numel, scale_b,
+                             scale_b_numel, bias, m, n, k, lda, ldb, ldo, 0u, nullptr, tile_n,
+                             tmw::as_stream(stream), &spec);
 }
 
 int tm_scaled_mm_i8_tile(void* out, int out_dtype, const int8_t* a, const int8_t* b,

@@ -7,9 +7,11 @@ the same linears inside its DiT block, model/layers.py:346-368, :502-523):
 * ``TPW8A8MLP``        fc1 column-parallel (+bias, GELU-tanh in the GEMM
                        epilogue) -> per-token quant over the local K ->
                        fc2 row-parallel, partials summed by a row reduce-scatter
-                       (or all-reduce).  The fc2 bias is added once, by TP rank 0
-                       inside its GEMM epilogue, which makes the sum equal to
-                       ``reduce(partial) + bias`` (linear.py:284-289).
+                       (NCCL, or fused into the GEMM epilogue over NVLink peer
+                       memory) or an all-reduce.  ``reduce(partial) + bias``
+                       (linear.py:284-289): the fused path adds the bias on the
+                       owner after the sum; the NCCL paths let TP rank 0 add it
+                       in its GEMM epilogue so that it enters the sum once.
 * ``TPW8A8AttnProj``   merged QKV column-parallel (each of Q, K, V sharded
                        separately, linear.py:207-215) and the row-parallel
                        out-projection with an all-reduce.
@@ -114,8 +116,8 @@ class TPW8A8MLP:
         t = ctx.tp_world_size
         if ffn % t or (reduce == "reduce_scatter" and tokens % t):
             raise ValueError("ffn and tokens must divide by the TP degree")
-        if reduce not in ("reduce_scatter", "all_reduce"):
-            raise ValueError("reduce must be 'reduce_scatter' or 'all_reduce'")
+        if reduce not in ("reduce_scatter", "all_reduce", "fused_reduce_scatter"):
+            raise ValueError("reduce must be 'reduce_scatter', 'fused_reduce_scatter' or 'all_reduce'")
         self.ctx, self.tokens, self.d, self.ffn, self.reduce = ctx, tokens, d, ffn, reduce
         self.fc1 = column_weight(ffn, d, ctx, seed + 10, device, bias=True)
         self.fc2 = row_weight(d, ffn, ctx, seed + 20, device, bias=True)
@@ -124,16 +126,24 @@ class TPW8A8MLP:
         self.h = torch.empty(tokens, local_ffn, dtype=torch.bfloat16, device=device)
         self.q2 = _Quant(tokens, local_ffn, device)
         self.partial = torch.empty(tokens, d, dtype=torch.bfloat16, device=device)
-        rows_out = tokens // t if reduce == "reduce_scatter" and t > 1 else tokens
+        scatter = reduce in ("reduce_scatter", "fused_reduce_scatter")
+        rows_out = tokens // t if scatter and t > 1 else tokens
         self.out = torch.empty(rows_out, d, dtype=torch.bfloat16, device=device)
+        self.peer = None
+        if reduce == "fused_reduce_scatter" and t > 1:
+            from .peer_reduce import PeerReduceScatter
+
+            self.peer = PeerReduceScatter(ctx, tokens, d, device)
 
     @property
     def int8_ops(self) -> int:
         """Whole-job int8 GEMM operations of one forward (2 M N K per linear)."""
         return 2 * 2 * self.tokens * self.d * self.ffn
 
-    # our kernel launches per forward: 2 quant + 2 GEMM
-    launches_per_step = 4
+    @property
+    def launches_per_step(self) -> int:
+        """This package's kernel launches per forward: 2 quant + 2 GEMM (+1 owner reduction)."""
+        return 5 if self.peer is not None else 4
 
     def forward(self, x: torch.Tensor, gemm_events: list | None = None) -> torch.Tensor:
         self.q1(x)
@@ -143,9 +153,15 @@ class TPW8A8MLP:
         if gemm_events is not None:
             gemm_events[1].record()
         self.q2(self.h)
-        bias2 = self.fc2.bias if self.ctx.tp_rank == 0 else None
         if gemm_events is not None:
             gemm_events[2].record()
+        if self.peer is not None:
+            # fc2 partial blocks go straight to their owners; bias added once there
+            self.peer(self.q2.q, self.q2.s, self.fc2.q, self.fc2.scale, self.fc2.bias, self.out)
+            if gemm_events is not None:
+                gemm_events[3].record()
+            return self.out
+        bias2 = self.fc2.bias if self.ctx.tp_rank == 0 else None
         _gemm(self.q2, self.fc2, self.partial, bias=bias2)
         if gemm_events is not None:
             gemm_events[3].record()

@@ -1,0 +1,127 @@
+"""Fused row-parallel reduce-scatter over NVLink peer memory.
+
+The row-parallel linears of the reference sum their partial outputs with an
+NCCL all-reduce after the GEMM (src/taomate_hd/distributed/linear.py:279-289,
+collectives.py:19-40).  ``PeerReduceScatter`` instead has the scaled-GEMM
+epilogue store each bf16 partial block directly into the rank that owns
+those rows, then sums the arrived blocks on the owner
+(``tm_scaled_mm_i8_reduce_scatter`` in ``include/taomate_w8a8.h``).
+
+Each rank allocates one buffer holding two sets (alternate calls) of
+``world`` receive slots of ``rows/world x cols`` bf16 plus their flags,
+shares it by CUDA IPC handle over the TP process group, and maps every
+peer's buffer once.  All ranks must call in the same order with the same
+shapes; the call counter (epoch) is kept identically on every rank.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import _native
+from .parallel import ParallelContext
+
+
+def _align(value: int, to: int = 256) -> int:
+    return (value + to - 1) // to * to
+
+
+class PeerReduceScatter:
+    """Symmetric receive buffers + the fused GEMM/reduce-scatter for one shape."""
+
+    def __init__(self, ctx: ParallelContext, rows: int, cols: int, device: torch.device):
+        world, rank = ctx.tp_world_size, ctx.tp_rank
+        if world < 1 or world > 8:
+            raise ValueError("the fused reduce-scatter supports 1..8 ranks")
+        if rows % (256 * world):
+            raise ValueError(f"rows ({rows}) must be a multiple of 256 * world ({256 * world})")
+        if cols % 16:
+            raise ValueError("cols must be a multiple of 16")
+        self.ctx, self.rows, self.cols, self.device = ctx, rows, cols, device
+        self.world, self.rank = world, rank
+        self.rows_per_owner = rows // world
+        self._lib = _native.capi()
+        recv_bytes = _align(world * self.rows_per_owner * cols * 2)
+        flag_bytes = _align(world * (self.rows_per_owner // 128) * math.ceil(cols / 64) * 4)
+        self._half = recv_bytes + flag_bytes
+        self._recv_bytes = recv_bytes
+        handle_size = self._lib.tm_peer_handle_size()
+        handle = (ctypes.c_char * handle_size)()
+        base = ctypes.c_void_p()
+        with torch.cuda.device(device):
+            rc = self._lib.tm_peer_alloc(2 * self._half, ctypes.byref(base), handle)
+            if rc != 0:
+                raise RuntimeError(f"tm_peer_alloc failed: {self._lib.tm_status_string(rc).decode()}")
+            torch.cuda.synchronize(device)
+        self._own = base.value
+        self._opened: list[int] = []
+        bases = [0] * world
+        bases[rank] = self._own
+        if world > 1:
+            gathered: list[bytes | None] = [None] * world
+            torch.distributed.all_gather_object(gathered, bytes(handle), group=ctx.tp_group)
+            with torch.cuda.device(device):
+                for j, h in enumerate(gathered):
+                    if j == rank:
+                        continue
+                    ptr = ctypes.c_void_p()
+                    buf = (ctypes.c_char * handle_size).from_buffer_copy(h)
+                    rc = self._lib.tm_peer_open(buf, ctypes.byref(ptr))
+                    if rc != 0:
+                        self.close()
+                        raise RuntimeError(
+                            f"tm_peer_open(rank {j}) failed: {self._lib.tm_status_string(rc).decode()}")
+                    bases[j] = ptr.value
+                    self._opened.append(ptr.value)
+            torch.distributed.barrier(group=ctx.tp_group)
+        arr = ctypes.c_void_p * world
+        self._recv = [arr(*[b + h * self._half for b in bases]) for h in (0, 1)]
+        self._flags = [arr(*[b + h * self._half + recv_bytes for b in bases]) for h in (0, 1)]
+        self.epoch = 0
+
+    def __call__(self, q: torch.Tensor, q_scale: torch.Tensor, w_q: torch.Tensor,
+                 w_scale: torch.Tensor, bias: torch.Tensor | None, out: torch.Tensor,
+                 tile_n: int = 0) -> torch.Tensor:
+        """``out[rows/world, cols] = (sum over ranks of this row block of q @ w_q^T) + bias``.
+
+        ``q``: int8 ``[rows, k]`` local activations; ``q_scale``: fp32 per-token
+        (or one) scales; ``w_q``: int8 ``[cols, k]`` local weight shard;
+        ``w_scale``: fp32 ``[cols]``; ``bias``: bf16 ``[cols]`` or None.
+        """
+        m, k = q.shape
+        if m != self.rows or w_q.shape[0] != self.cols or w_q.shape[1] != k:
+            raise ValueError("shape differs from the one the buffers were built for")
+        if out.shape != (self.rows_per_owner, self.cols) or out.dtype != torch.bfloat16:
+            raise ValueError(f"out must be bf16 [{self.rows_per_owner}, {self.cols}]")
+        self.epoch += 1
+        half = self.epoch & 1
+        stream = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+        rc = self._lib.tm_scaled_mm_i8_reduce_scatter(
+            out.data_ptr(), q.data_ptr(), w_q.data_ptr(), q_scale.data_ptr(), q_scale.numel(),
+            w_scale.data_ptr(), w_scale.numel(), None if bias is None else bias.data_ptr(),
+            m, self.cols, k, q.stride(0), w_q.stride(0), out.stride(0),
+            self._recv[half], self._flags[half], self.world, self.rank, self.epoch & 0xFFFFFFFF,
+            tile_n, stream)
+        if rc != 0:
+            raise RuntimeError(
+                f"tm_scaled_mm_i8_reduce_scatter failed: {self._lib.tm_status_string(rc).decode()}")
+        return out
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (after a device sync)."""
+        if getattr(self, "_own", None) is None:
+            return
+        torch.cuda.synchronize(self.device)
+        for ptr in self._opened:
+            self._lib.tm_peer_close(ctypes.c_void_p(ptr))
+        self._opened = []
+        self._lib.tm_peer_free(ctypes.c_void_p(self._own))
+        self._own = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
