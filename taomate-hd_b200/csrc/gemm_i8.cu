@@ -121,10 +121,15 @@ __device__ __forceinline__ float round_out<__half>(float v) {
   return __half2float(__float2half_rn(v));
 }
 
-// Epilogue for 16 consecutive columns held in r[0..15] of one row.
+// Dequantise 16 consecutive columns held in r[0..15] of one row and pack
+// them into two 16-byte words of OutT.  Columns past N are never stored.
 template <typename OutT>
 __device__ __forceinline__ void epilogue16(const GemmArgs& g, const uint32_t* r, float sa,
-                                           OutT* out_row, int32_t* dbg_row, int col) {
+                                           int col, uint4& o0, uint4& o1) {
+  if (col >= g.N) {
+    o0 = o1 = make_uint4(0, 0, 0, 0);
+    return;
+  }
   float sb[16];
   if (g.sb_per_col) {
     const float4* p = reinterpret_cast<const float4*>(g.sb + col);
@@ -163,7 +168,6 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& g, const uint32_t* r,
 #pragma unroll
     for (int j = 0; j < 16; ++j) y[j] = gelu_tanh(round_out<OutT>(y[j]));
   }
-  uint4 o0, o1;
   o0.x = pack2<OutT>(y[0], y[1]);
   o0.y = pack2<OutT>(y[2], y[3]);
   o0.z = pack2<OutT>(y[4], y[5]);
@@ -172,52 +176,85 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& g, const uint32_t* r,
   o1.y = pack2<OutT>(y[10], y[11]);
   o1.z = pack2<OutT>(y[12], y[13]);
   o1.w = pack2<OutT>(y[14], y[15]);
-  uint4* dst = reinterpret_cast<uint4*>(out_row + col);
-  dst[0] = o0;
-  dst[1] = o1;
-  if (dbg_row != nullptr) {
-    uint4* d = reinterpret_cast<uint4*>(dbg_row + col);
-    d[0] = make_uint4(r[0], r[1], r[2], r[3]);
-    d[1] = make_uint4(r[4], r[5], r[6], r[7]);
-    d[2] = make_uint4(r[8], r[9], r[10], r[11]);
-    d[3] = make_uint4(r[12], r[13], r[14], r[15]);
+}
+
+// Output row pointer: the row itself, or (scatter mode) its owner's slot.
+template <typename OutT>
+__device__ __forceinline__ OutT* out_row_ptr(const GemmArgs& g, int64_t row) {
+  if (g.world > 0) {
+    const int owner = static_cast<int>(row / g.rows_per_owner);
+    const int64_t local = row - static_cast<int64_t>(owner) * g.rows_per_owner;
+    return reinterpret_cast<OutT*>(g.peer_recv[owner]) +
+           (static_cast<int64_t>(g.rank) * g.rows_per_owner + local) * g.N;
   }
+  return static_cast<OutT*>(g.out) + row * g.ldo;
+}
+
+// Per-warp staging tile: 32 rows x 128 bytes, 16-byte chunks XOR-swizzled by
+// row so that both the row-per-lane writes and the row-segment reads are
+// free of bank conflicts.
+constexpr int kStageRowBytes = 128;
+constexpr int kEpiStageBytes = 32 * kStageRowBytes;  // per epilogue warp
+
+__device__ __forceinline__ uint4* stage_slot(uint8_t* stage, int row, int chunk) {
+  return reinterpret_cast<uint4*>(stage + row * kStageRowBytes + ((chunk ^ (row & 7)) << 4));
 }
 
 // One epilogue warp's share of a 128 x BN accumulator held in this CTA's
 // TMEM at column `acc_col`: lane quarter warp % 4, column half (warp-2)/4.
+// Each group of 64 columns is dequantised (lane = row), staged in shared
+// memory, and written back as 128-byte row segments (8 lanes per row), so
+// global and NVLink peer stores are full-line writes.
 template <int BN, typename OutT>
 __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tmem_base,
                                               uint32_t acc_col, int64_t row0, int col0,
-                                              int warp, int lane) {
+                                              int warp, int lane, uint8_t* stage) {
   constexpr int kHalf = BN / 2;
+  constexpr int kColsPerPass = kStageRowBytes / sizeof(OutT);  // 64
   const int q = warp & 3;
   const int h = (warp - 2) >> 2;
-  const int64_t row = row0 + q * 32 + lane;
+  const int64_t row_base = row0 + q * 32;
+  const int64_t row = row_base + lane;
   const bool row_ok = row < g.M;
   const float sa = row_ok ? (g.sa_per_row ? __ldg(g.sa + row) : __ldg(g.sa)) : 0.f;
-  OutT* out_row;
-  if (g.world > 0) {
-    const int owner = row_ok ? static_cast<int>(row / g.rows_per_owner) : 0;
-    const int64_t local = row - static_cast<int64_t>(owner) * g.rows_per_owner;
-    out_row = reinterpret_cast<OutT*>(g.peer_recv[owner]) +
-              (static_cast<int64_t>(g.rank) * g.rows_per_owner + local) * g.N;
-  } else {
-    out_row = static_cast<OutT*>(g.out) + row * g.ldo;
-  }
-  int32_t* dbg_row = g.acc_debug != nullptr ? g.acc_debug + row * static_cast<int64_t>(g.N) : nullptr;
+  int32_t* dbg_row = (g.acc_debug != nullptr && row_ok)
+                         ? g.acc_debug + row * static_cast<int64_t>(g.N) : nullptr;
   const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc_col +
                          static_cast<uint32_t>(h * kHalf);
 #pragma unroll 1
-  for (int c = 0; c < kHalf / 32; ++c) {
-    uint32_t r[32];
-    tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c * 32), r);
-    tmem_ld_wait();
-    const int col = col0 + h * kHalf + c * 32;
-    if (row_ok) {
-      if (col < g.N) epilogue16<OutT>(g, r, sa, out_row, dbg_row, col);
-      if (col + 16 < g.N) epilogue16<OutT>(g, r + 16, sa, out_row, dbg_row, col + 16);
+  for (int pass = 0; pass * kColsPerPass < kHalf; ++pass) {
+    const int pass_cols = min(kColsPerPass, kHalf - pass * kColsPerPass);  // 64 or 32
+    const int pass_col0 = col0 + h * kHalf + pass * kColsPerPass;
+#pragma unroll 1
+    for (int c = 0; c < pass_cols / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(pass * kColsPerPass + c * 32), r);
+      tmem_ld_wait();
+      const int col = pass_col0 + c * 32;
+      uint4 o[4];
+      epilogue16<OutT>(g, r, sa, col, o[0], o[1]);
+      epilogue16<OutT>(g, r + 16, sa, col + 16, o[2], o[3]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) *stage_slot(stage, lane, c * 4 + j) = o[j];
+      if (dbg_row != nullptr) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4)
+          if (col + j < g.N)
+            *reinterpret_cast<uint4*>(dbg_row + col + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+      }
     }
+    __syncwarp();
+    const int chunks = pass_cols * static_cast<int>(sizeof(OutT)) / 16;  // 8 or 4 per row
+    const int rows_per_store = 32 / chunks;
+    const int chunk = lane % chunks;
+#pragma unroll 1
+    for (int rr = lane / chunks; rr < 32; rr += rows_per_store) {
+      const int64_t out_r = row_base + rr;
+      const int col = pass_col0 + chunk * (16 / static_cast<int>(sizeof(OutT)));
+      if (out_r < g.M && col < g.N)
+        *reinterpret_cast<uint4*>(out_row_ptr<OutT>(g, out_r) + col) = *stage_slot(stage, rr, chunk);
+    }
+    __syncwarp();
   }
 }
 
@@ -247,7 +284,8 @@ struct Smem {
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kBarOffset = STAGES * kStageBytes;
   static constexpr int kBarBytes = (2 * STAGES + 4) * 8 + 16;
-  static constexpr int kTotal = kBarOffset + kBarBytes + 1024;  // + alignment slack
+  static constexpr int kEpiOffset = (kBarOffset + kBarBytes + 127) / 128 * 128;
+  static constexpr int kTotal = kEpiOffset + kEpiWarps * kEpiStageBytes + 1024;  // + align slack
   static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "swizzle atoms need 1 KiB alignment");
   static_assert(kTotal <= 227 * 1024, "shared memory budget");
 };
@@ -410,7 +448,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&bar.tmem_full[acc], acc_phase, bar.abort_flag, g.status)) break;
       tc_fence_after();
       epilogue_tile<BN, OutT>(g, tmem_base, static_cast<uint32_t>(acc * BN),
-                              static_cast<int64_t>(mb) * kBM, nb * BN, warp, lane);
+                              static_cast<int64_t>(mb) * kBM, nb * BN, warp, lane,
+                              smem + L::kEpiOffset + (warp - 2) * kEpiStageBytes);
       if (g.world > 0 && static_cast<int64_t>(mb) * kBM < g.M)
         publish_block(g, static_cast<int64_t>(mb) * kBM, nb, warp, lane);
       tc_fence_before();
@@ -587,7 +626,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int64_t row0 = static_cast<int64_t>(mb) * 2 * kBM + rank * kBM;
       epilogue_tile<BN, OutT>(g, tmem_base, static_cast<uint32_t>(acc * BN), row0, nb * BN, warp,
-                              lane);
+                              lane, smem + L::kEpiOffset + (warp - 2) * kEpiStageBytes);
       if (g.world > 0 && row0 < g.M) publish_block(g, row0, nb, warp, lane);
       tc_fence_before();
       __syncwarp();
@@ -680,7 +719,7 @@ int dispatch(const Operands& op, const GemmArgs& args, int cfg, int sms, int max
     case 128: return launch_single<128, 6, OutT>(op, args, sms, stream);
     case 64: return launch_single<64, 8, OutT>(op, args, sms, stream);
     case kPairFlag + 256: return launch_pair<256, 6, OutT>(op, args, max_pairs, stream);
-    case kPairFlag + 192: return launch_pair<192, 7, OutT>(op, args, max_pairs, stream);
+    case kPairFlag + 192: return launch_pair<192, 6, OutT>(op, args, max_pairs, stream);
     case kPairFlag + 128: return launch_pair<128, 8, OutT>(op, args, max_pairs, stream);
     default: return TM_ERR_UNSUPPORTED;
   }
