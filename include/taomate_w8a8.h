@@ -138,21 +138,22 @@ int tm_scaled_mm_i8_tile(void* out, int out_dtype, const int8_t* a, const int8_t
                          int32_t* acc_debug, int tile_n, void* stream);
 
 /*
- * Row-parallel scaled GEMM with the reduce-scatter fused into its epilogue
+ * Row-parallel scaled GEMM with the reduce-scatter fused into the kernel
  * (the row-parallel fc2 / out-projection; the reference's
  * RowParallelLinear.forward = forward_local + tp all-reduce + bias,
  * src/taomate_hd/distributed/linear.py:259-289 and collectives.py:19-40).
  * Every rank of a TP group of `world` ranks calls it with its K-shard
  * (a: [m, k] local activations, b: the [n, k] local weight).  Rows are
  * owned in `world` contiguous blocks of m / world (m % (256 * world) == 0).
- * The epilogue stores each bf16 partial 128-row block straight into its
- * owner's receive buffer peer_recv[owner] (slot `rank`) over NVLink and
- * publishes `epoch` in peer_flags[owner]; then this rank waits (bounded) for
- * its own rows from every source, sums them in rank order in fp32, adds
- * `bias` ([n] bf16 or NULL) once and writes out[m / world, n] (row stride ldo).
- * peer_recv[j]: device pointer (local or IPC-mapped) to rank j's buffer of
- *   world * (m / world) * n bf16;  peer_flags[j]: rank j's flag array of
- *   world * (m / world / 128) * ceil(n / 64) uint32 (zeroed once).
+ * The epilogue writes this rank's bf16 partial [m, n] into
+ * peer_part[rank] and publishes `epoch` per 128-row block in
+ * peer_flags[rank]; CTAs that run out of GEMM tiles then wait (bounded) for
+ * every source's blocks of this rank's rows, pull them from peer_part[src]
+ * (NVLink loads), sum in rank order in fp32, add `bias` ([n] bf16 or NULL)
+ * once and write out[m / world, n] (row stride ldo).
+ * peer_part[j]: device pointer (local or IPC-mapped) to rank j's partial
+ *   buffer of m * n bf16; peer_flags[j]: rank j's flag array of
+ *   (m / 128) * ceil(n / 64) uint32, zeroed once at allocation.
  * epoch: a call counter identical on all ranks, never 0; consecutive calls
  * must alternate between two buffer sets (a rank may run one call ahead).
  * tile_n: 0 for the heuristic or a tm_scaled_mm_i8_tile configuration.
@@ -162,7 +163,7 @@ int tm_scaled_mm_i8_reduce_scatter(void* out, const int8_t* a, const int8_t* b,
                                    const float* scale_a, int64_t scale_a_numel,
                                    const float* scale_b, int64_t scale_b_numel, const void* bias,
                                    int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
-                                   int64_t ldo, void* const* peer_recv, void* const* peer_flags,
+                                   int64_t ldo, void* const* peer_part, void* const* peer_flags,
                                    int world, int rank, uint32_t epoch, int tile_n, void* stream);
 
 /*

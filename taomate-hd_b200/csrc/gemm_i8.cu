@@ -33,7 +33,6 @@
 #include <cmath>
 
 #include "common.h"
-#include "peer_reduce.h"
 #include "ptx.cuh"
 
 namespace tmw {
@@ -44,6 +43,7 @@ constexpr int kBK = 128;  // bytes == int8 elements of K per k-block (one swizzl
 constexpr int kThreads = 320;
 constexpr int kEpiWarps = 8;
 constexpr int kGroupM = 16;
+constexpr int kMaxPeers = 8;
 
 struct GemmArgs {
   const float* sa;
@@ -58,13 +58,21 @@ struct GemmArgs {
   int num_m, num_n, kblocks;  // tile grid (in units of the kernel's tile)
   uint32_t epilogue;
   int* status;
-  // Row-parallel scatter (fused reduce-scatter); world == 0 disables it.
-  // Rows of owner j (j * rows_per_owner ...) go to peer_recv[j] slot `rank`;
-  // each finished 128-row x tile-width block publishes `epoch` in
-  // peer_flags[j][rank][row block][column tile].
+  // Row-parallel fused reduce-scatter; world == 0 disables it.  Rank j owns
+  // rows [j * rows_per_owner, +rows_per_owner).  The epilogue stores each
+  // bf16 partial block of owner j's rows into peer_part[j], slot `rank`
+  // ([world][rows_per_owner][N], an NVLink peer store unless j == rank), and
+  // publishes `epoch` for the 128-row x tile-width block in peer_flags[j]
+  // ([world][rows_per_owner/128][num_n]).  CTAs that run out of GEMM tiles
+  // then reduce this rank's rows from its own slots (local HBM reads): wait
+  // for each source's block flag, sum in rank order, add red_bias, store to
+  // red_out.
   int world, rank, rows_per_owner;
   uint32_t epoch;
-  __nv_bfloat16* peer_recv[kMaxPeers];
+  const __nv_bfloat16* red_bias;
+  __nv_bfloat16* red_out;
+  int64_t red_ldo;
+  __nv_bfloat16* peer_part[kMaxPeers];
   uint32_t* peer_flags[kMaxPeers];
 };
 
@@ -184,7 +192,7 @@ __device__ __forceinline__ OutT* out_row_ptr(const GemmArgs& g, int64_t row) {
   if (g.world > 0) {
     const int owner = static_cast<int>(row / g.rows_per_owner);
     const int64_t local = row - static_cast<int64_t>(owner) * g.rows_per_owner;
-    return reinterpret_cast<OutT*>(g.peer_recv[owner]) +
+    return reinterpret_cast<OutT*>(g.peer_part[owner]) +
            (static_cast<int64_t>(g.rank) * g.rows_per_owner + local) * g.N;
   }
   return static_cast<OutT*>(g.out) + row * g.ldo;
@@ -262,18 +270,149 @@ __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Scatter mode: after all 8 epilogue warps stored a 128-row block of the
-// tile into its owner's receive slot, publish the block's flag on the owner.
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint4 ld_cg16(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+// Fused reduce-scatter: once all 8 epilogue warps have issued the stores of
+// a 128-row block into its owner's slot, one thread publishes the block's
+// flag on the owner.  The named barrier orders every warp's stores before
+// that thread's system-scope fence and release store (fences are cumulative),
+// so only one thread waits for the stores to land.
 __device__ __forceinline__ void publish_block(const GemmArgs& g, int64_t row0, int nb, int warp,
                                               int lane) {
-  __threadfence_system();
   asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
   if (warp == 2 && lane == 0) {
     const int owner = static_cast<int>(row0 / g.rows_per_owner);
     const int lrb = static_cast<int>((row0 - static_cast<int64_t>(owner) * g.rows_per_owner) / kBM);
-    uint32_t* f = g.peer_flags[owner] +
-                  (static_cast<int64_t>(g.rank) * (g.rows_per_owner / kBM) + lrb) * g.num_n + nb;
-    st_release_sys(f, g.epoch);
+    __threadfence_system();
+    st_release_sys(g.peer_flags[owner] +
+                       (static_cast<int64_t>(g.rank) * (g.rows_per_owner / kBM) + lrb) * g.num_n +
+                       nb,
+                   g.epoch);
+  }
+}
+
+// Flag values are call epochs; "reached" is a wrap-safe epoch comparison.
+__device__ __forceinline__ bool epoch_reached(uint32_t flag, uint32_t epoch) {
+  return static_cast<int32_t>(flag - epoch) >= 0;
+}
+
+// Sum one block's partials from `world` (<= W) source slots, V vectors of 8
+// columns per thread per round: all V x world 16-byte loads of a round are
+// issued before any is consumed, keeping ~32 registers of NVLink loads in
+// flight per thread (3-5 MB across the GPU, enough to keep NVLink busy).
+template <int V, int W>
+__device__ __forceinline__ void reduce_block(const GemmArgs& g, int lrb, int col0,
+                                             int vec_per_row) {
+  const int total = kBM * vec_per_row;
+  for (int v0 = threadIdx.x; v0 < total; v0 += V * blockDim.x) {
+    uint4 raw[V][W];
+    int64_t off[V];
+#pragma unroll
+    for (int u = 0; u < V; ++u) {
+      const int v = v0 + u * static_cast<int>(blockDim.x);
+      const int vv = v < total ? v : v0;
+      const int r = vv / vec_per_row;
+      off[u] = (static_cast<int64_t>(lrb) * kBM + r) * g.N + col0 + (vv - r * vec_per_row) * 8;
+    }
+    const __nv_bfloat16* slots = g.peer_part[g.rank];
+    const int64_t slot_elems = static_cast<int64_t>(g.rows_per_owner) * g.N;
+#pragma unroll
+    for (int src = 0; src < W; ++src)
+      if (src < g.world) {
+#pragma unroll
+        for (int u = 0; u < V; ++u) raw[u][src] = ld_cg16(slots + src * slot_elems + off[u]);
+      }
+#pragma unroll
+    for (int u = 0; u < V; ++u) {
+      const int v = v0 + u * static_cast<int>(blockDim.x);
+      if (v >= total) continue;
+      const int r = v / vec_per_row;
+      const int c = col0 + (v - r * vec_per_row) * 8;
+      float acc[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+#pragma unroll
+      for (int src = 0; src < W; ++src)
+        if (src < g.world) {
+          const __nv_bfloat162* hp = reinterpret_cast<const __nv_bfloat162*>(&raw[u][src]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = __bfloat1622float2(hp[j]);
+            acc[2 * j] = __fadd_rn(acc[2 * j], f.x);
+            acc[2 * j + 1] = __fadd_rn(acc[2 * j + 1], f.y);
+          }
+        }
+      if (g.red_bias != nullptr) {
+        const uint4 braw = __ldg(reinterpret_cast<const uint4*>(g.red_bias + c));
+        const __nv_bfloat162* bp = reinterpret_cast<const __nv_bfloat162*>(&braw);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(bp[j]);
+          acc[2 * j] = __fadd_rn(acc[2 * j], f.x);
+          acc[2 * j + 1] = __fadd_rn(acc[2 * j + 1], f.y);
+        }
+      }
+      uint4 o;
+      __nv_bfloat162* op = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) op[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
+      *reinterpret_cast<uint4*>(g.red_out + (static_cast<int64_t>(lrb) * kBM + r) * g.red_ldo + c) = o;
+    }
+  }
+}
+
+// Fused reduce-scatter, owner side, run by every thread of a CTA that has no
+// GEMM tiles left (all CTAs of the cooperative persistent grid are resident,
+// and peers run concurrently on their own GPUs, so every wait here is on work
+// that is already executing).  Block (row block, column tile) of this rank's
+// rows: wait for all sources' flags, read the bf16 partials the sources
+// pushed into this rank's slots (local HBM), sum in rank order in fp32, add
+// the bias, store.  Waits are bounded; a timeout records the device status
+// and skips the block.
+__device__ void reduce_phase(const GemmArgs& g, int bn, int cta, int ctas) {
+  const int rbpo = g.rows_per_owner / kBM;
+  const int tiles = rbpo * g.num_n;
+  for (int t = cta; t < tiles; t += ctas) {
+    const int lrb = t / g.num_n;
+    const int nb = t - lrb * g.num_n;
+    int ok = 1;
+    if (threadIdx.x < static_cast<unsigned>(g.world)) {
+      const uint32_t* f =
+          g.peer_flags[g.rank] + (static_cast<int64_t>(threadIdx.x) * rbpo + lrb) * g.num_n + nb;
+      bool seen = epoch_reached(ld_acquire_sys(f), g.epoch);
+      if (!seen) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!(seen = epoch_reached(ld_acquire_sys(f), g.epoch))) {
+          if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+          __nanosleep(32);
+        }
+      }
+      if (!seen) {
+        ok = 0;
+        if (g.status) atomicExch(g.status, kDevWaitTimeout);
+      }
+    }
+    if (!__syncthreads_and(ok)) continue;
+    const int col0 = nb * bn;
+    const int vec_per_row = min(bn, g.N - col0) / 8;
+    if (g.world <= 2)
+      reduce_block<4, 2>(g, lrb, col0, vec_per_row);
+    else if (g.world <= 4)
+      reduce_block<2, 4>(g, lrb, col0, vec_per_row);
+    else
+      reduce_block<1, 8>(g, lrb, col0, vec_per_row);
   }
 }
 
@@ -450,11 +589,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       epilogue_tile<BN, OutT>(g, tmem_base, static_cast<uint32_t>(acc * BN),
                               static_cast<int64_t>(mb) * kBM, nb * BN, warp, lane,
                               smem + L::kEpiOffset + (warp - 2) * kEpiStageBytes);
-      if (g.world > 0 && static_cast<int64_t>(mb) * kBM < g.M)
-        publish_block(g, static_cast<int64_t>(mb) * kBM, nb, warp, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar.tmem_empty[acc]);
+      if (g.world > 0 && static_cast<int64_t>(mb) * kBM < g.M)
+        publish_block(g, static_cast<int64_t>(mb) * kBM, nb, warp, lane);
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
@@ -468,6 +607,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, 2 * BN);
   }
+  if (g.world > 0) reduce_phase(g, BN, blockIdx.x, gridDim.x);
 }
 
 // ====================================================================== CTA pair
@@ -627,10 +767,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t row0 = static_cast<int64_t>(mb) * 2 * kBM + rank * kBM;
       epilogue_tile<BN, OutT>(g, tmem_base, static_cast<uint32_t>(acc * BN), row0, nb * BN, warp,
                               lane, smem + L::kEpiOffset + (warp - 2) * kEpiStageBytes);
-      if (g.world > 0 && row0 < g.M) publish_block(g, row0, nb, warp, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc == 0 ? empty_leader0 : empty_leader1);
+      if (g.world > 0 && row0 < g.M) publish_block(g, row0, nb, warp, lane);
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
@@ -644,6 +784,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, PairTmem<BN>::kCols);
   }
+  if (g.world > 0) reduce_phase(g, BN, blockIdx.x, gridDim.x);
 }
 
 // ====================================================================== host
@@ -670,7 +811,19 @@ int launch_single(const Operands& op, GemmArgs args, int sms, cudaStream_t strea
       cudaSuccess)
     return TM_ERR_CUDA;
   const int tiles = args.num_m * args.num_n;
-  kernel<<<tiles < sms ? tiles : sms, kThreads, L::kTotal, stream>>>(ta, tb, args);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(tiles < sms ? tiles : sms));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = L::kTotal;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  // The fused reduce-scatter waits on blocks produced by other CTAs of the
+  // same launch: require them all to be resident at once.
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = args.world > 0 ? 1 : 0;
+  if (cudaLaunchKernelEx(&cfg, kernel, ta, tb, args) != cudaSuccess) return TM_ERR_CUDA;
   return check_launch();
 }
 
@@ -696,13 +849,17 @@ int launch_pair(const Operands& op, GemmArgs args, int max_pairs, cudaStream_t s
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = L::kTotal;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // The fused reduce-scatter waits on blocks produced by other CTAs of the
+  // same launch: require them all to be resident at once.
+  attr[1].id = cudaLaunchAttributeCooperative;
+  attr[1].val.cooperative = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = args.world > 0 ? 2 : 1;
   if (cudaLaunchKernelEx(&cfg, kernel, ta, tb, args) != cudaSuccess) return TM_ERR_CUDA;
   return check_launch();
 }
@@ -797,7 +954,7 @@ int max_resident_pairs(int device, int sms) {
 // Fused reduce-scatter request (row-parallel linears); see
 // tm_scaled_mm_i8_reduce_scatter.
 struct ScatterSpec {
-  void* const* peer_recv;
+  void* const* peer_part;
   void* const* peer_flags;
   int world;
   int rank;
@@ -823,10 +980,10 @@ int scaled_mm_impl(void* out, int out_dtype, const int8_t* a, const int8_t* b, c
     if (scatter->rank < 0 || scatter->rank >= scatter->world) return TM_ERR_SHAPE;
     if (m % (static_cast<int64_t>(scatter->world) * 2 * kBM) != 0) return TM_ERR_SHAPE;
     if (out_dtype != TM_DTYPE_BF16 || epilogue != 0) return TM_ERR_UNSUPPORTED;
-    if (!scatter->peer_recv || !scatter->peer_flags) return TM_ERR_NULL_POINTER;
+    if (!scatter->peer_part || !scatter->peer_flags) return TM_ERR_NULL_POINTER;
     for (int j = 0; j < scatter->world; ++j) {
-      if (!scatter->peer_recv[j] || !scatter->peer_flags[j]) return TM_ERR_NULL_POINTER;
-      if (!aligned16(scatter->peer_recv[j]) || !aligned16(scatter->peer_flags[j]))
+      if (!scatter->peer_part[j] || !scatter->peer_flags[j]) return TM_ERR_NULL_POINTER;
+      if (!aligned16(scatter->peer_part[j]) || !aligned16(scatter->peer_flags[j]))
         return TM_ERR_ALIGNMENT;
     }
   }
@@ -859,8 +1016,11 @@ int scaled_mm_impl(void* out, int out_dtype, const int8_t* a, const int8_t* b, c
     args.rank = scatter->rank;
     args.rows_per_owner = static_cast<int>(m / scatter->world);
     args.epoch = scatter->epoch;
+    args.red_bias = static_cast<const __nv_bfloat16*>(bias);
+    args.red_out = static_cast<__nv_bfloat16*>(out);
+    args.red_ldo = ldo;
     for (int j = 0; j < scatter->world; ++j) {
-      args.peer_recv[j] = static_cast<__nv_bfloat16*>(scatter->peer_recv[j]);
+      args.peer_part[j] = static_cast<__nv_bfloat16*>(scatter->peer_part[j]);
       args.peer_flags[j] = static_cast<uint32_t*>(scatter->peer_flags[j]);
     }
   }
@@ -868,26 +1028,9 @@ int scaled_mm_impl(void* out, int out_dtype, const int8_t* a, const int8_t* b, c
   const int cfg = force_cfg ? force_cfg : pick_config(args.M, args.N, sms, max_pairs);
   if (cfg > kPairFlag && max_pairs <= 0) return TM_ERR_UNSUPPORTED;
   const Operands op{a, lda, b, ldb};
-  int status = out_dtype == TM_DTYPE_BF16
-                   ? dispatch<__nv_bfloat16>(op, args, cfg, sms, max_pairs, stream)
-                   : dispatch<__half>(op, args, cfg, sms, max_pairs, stream);
-  if (status != TM_OK || scatter == nullptr) return status;
-  // Owner side: wait for every source's blocks, sum in rank order, add bias.
-  const int bn = cfg > kPairFlag ? cfg - kPairFlag : cfg;
-  RsReduceArgs r{};
-  r.recv = static_cast<const __nv_bfloat16*>(scatter->peer_recv[scatter->rank]);
-  r.flags = static_cast<const uint32_t*>(scatter->peer_flags[scatter->rank]);
-  r.bias = static_cast<const __nv_bfloat16*>(bias);
-  r.out = static_cast<__nv_bfloat16*>(out);
-  r.ldo = ldo;
-  r.world = scatter->world;
-  r.rows_per_owner = args.rows_per_owner;
-  r.n = args.N;
-  r.tile_n = bn;
-  r.num_n = (args.N + bn - 1) / bn;
-  r.epoch = scatter->epoch;
-  r.status = args.status;
-  return launch_rs_reduce(r, stream);
+  if (out_dtype == TM_DTYPE_BF16)
+    return dispatch<__nv_bfloat16>(op, args, cfg, sms, max_pairs, stream);
+  return dispatch<__half>(op, args, cfg, sms, max_pairs, stream);
 }
 
 }  // namespace
@@ -917,9 +1060,9 @@ int tm_scaled_mm_i8_reduce_scatter(void* out, const int8_t* a, const int8_t* b,
                                    const float* scale_a, int64_t scale_a_numel,
                                    const float* scale_b, int64_t scale_b_numel, const void* bias,
                                    int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
-                                   int64_t ldo, void* const* peer_recv, void* const* peer_flags,
+                                   int64_t ldo, void* const* peer_part, void* const* peer_flags,
                                    int world, int rank, uint32_t epoch, int tile_n, void* stream) {
-  const tmw::ScatterSpec spec{peer_recv, peer_flags, world, rank, epoch};
+  const tmw::ScatterSpec spec{peer_part, peer_flags, world, rank, epoch};
   return tmw::scaled_mm_impl(out, TM_DTYPE_BF16, a, b, scale_a, scale_a_numel, scale_b,
                              scale_b_numel, bias, m, n, k, lda, ldb, ldo, 0u, nullptr, tile_n,
                              tmw::as_stream(stream), &spec);

@@ -140,10 +140,9 @@ class TPW8A8MLP:
         """Whole-job int8 GEMM operations of one forward (2 M N K per linear)."""
         return 2 * 2 * self.tokens * self.d * self.ffn
 
-    @property
-    def launches_per_step(self) -> int:
-        """This package's kernel launches per forward: 2 quant + 2 GEMM (+1 owner reduction)."""
-        return 5 if self.peer is not None else 4
+    # this package's kernel launches per forward: 2 quant + 2 GEMM (the fused
+    # reduce-scatter runs inside the fc2 GEMM launch)
+    launches_per_step = 4
 
     def forward(self, x: torch.Tensor, gemm_events: list | None = None) -> torch.Tensor:
         self.q1(x)

@@ -2,16 +2,18 @@
 
 The row-parallel linears of the reference sum their partial outputs with an
 NCCL all-reduce after the GEMM (src/taomate_hd/distributed/linear.py:279-289,
-collectives.py:19-40).  ``PeerReduceScatter`` instead has the scaled-GEMM
-epilogue store each bf16 partial block directly into the rank that owns
-those rows, then sums the arrived blocks on the owner
-(``tm_scaled_mm_i8_reduce_scatter`` in ``include/taomate_w8a8.h``).
+collectives.py:19-40).  ``PeerReduceScatter`` runs the reduction inside the
+scaled-GEMM kernel instead (``tm_scaled_mm_i8_reduce_scatter`` in
+``include/taomate_w8a8.h``): each rank writes its bf16 partial blocks to its
+own buffer and flags them; CTAs that finished their GEMM tiles pull this
+rank's rows from every rank's buffer over NVLink, sum and add the bias, so
+the transfer overlaps the GEMM's tail.
 
-Each rank allocates one buffer holding two sets (alternate calls) of
-``world`` receive slots of ``rows/world x cols`` bf16 plus their flags,
-shares it by CUDA IPC handle over the TP process group, and maps every
-peer's buffer once.  All ranks must call in the same order with the same
-shapes; the call counter (epoch) is kept identically on every rank.
+Each rank allocates one buffer holding two sets (alternate calls) of an
+``rows x cols`` bf16 partial plus its block flags, shares it by CUDA IPC
+handle over the TP process group, and maps every peer's buffer once.  All
+ranks must call in the same order with the same shapes; the call counter
+(epoch) is kept identically on every rank.
 """
 from __future__ import annotations
 
@@ -43,10 +45,9 @@ class PeerReduceScatter:
         self.world, self.rank = world, rank
         self.rows_per_owner = rows // world
         self._lib = _native.capi()
-        recv_bytes = _align(world * self.rows_per_owner * cols * 2)
-        flag_bytes = _align(world * (self.rows_per_owner // 128) * math.ceil(cols / 64) * 4)
-        self._half = recv_bytes + flag_bytes
-        self._recv_bytes = recv_bytes
+        part_bytes = _align(rows * cols * 2)
+        flag_bytes = _align((rows // 128) * math.ceil(cols / 64) * 4)
+        self._half = part_bytes + flag_bytes
         handle_size = self._lib.tm_peer_handle_size()
         handle = (ctypes.c_char * handle_size)()
         base = ctypes.c_void_p()
@@ -77,8 +78,8 @@ class PeerReduceScatter:
                     self._opened.append(ptr.value)
             torch.distributed.barrier(group=ctx.tp_group)
         arr = ctypes.c_void_p * world
-        self._recv = [arr(*[b + h * self._half for b in bases]) for h in (0, 1)]
-        self._flags = [arr(*[b + h * self._half + recv_bytes for b in bases]) for h in (0, 1)]
+        self._part = [arr(*[b + h * self._half for b in bases]) for h in (0, 1)]
+        self._flags = [arr(*[b + h * self._half + part_bytes for b in bases]) for h in (0, 1)]
         self.epoch = 0
 
     def __call__(self, q: torch.Tensor, q_scale: torch.Tensor, w_q: torch.Tensor,
@@ -102,7 +103,7 @@ class PeerReduceScatter:
             out.data_ptr(), q.data_ptr(), w_q.data_ptr(), q_scale.data_ptr(), q_scale.numel(),
             w_scale.data_ptr(), w_scale.numel(), None if bias is None else bias.data_ptr(),
             m, self.cols, k, q.stride(0), w_q.stride(0), out.stride(0),
-            self._recv[half], self._flags[half], self.world, self.rank, self.epoch & 0xFFFFFFFF,
+            self._part[half], self._flags[half], self.world, self.rank, self.epoch & 0xFFFFFFFF,
             tile_n, stream)
         if rc != 0:
             raise RuntimeError(
