@@ -145,18 +145,20 @@ int tm_scaled_mm_i8_tile(void* out, int out_dtype, const int8_t* a, const int8_t
  * Every rank of a TP group of `world` ranks calls it with its K-shard
  * (a: [m, k] local activations, b: the [n, k] local weight).  Rows are
  * owned in `world` contiguous blocks of m / world (m % (256 * world) == 0).
- * The epilogue writes this rank's bf16 partial [m, n] into
- * peer_part[rank] and publishes `epoch` per 128-row block in
- * peer_flags[rank]; CTAs that run out of GEMM tiles then wait (bounded) for
- * every source's blocks of this rank's rows, pull them from peer_part[src]
- * (NVLink loads), sum in rank order in fp32, add `bias` ([n] bf16 or NULL)
- * once and write out[m / world, n] (row stride ldo).
- * peer_part[j]: device pointer (local or IPC-mapped) to rank j's partial
- *   buffer of m * n bf16; peer_flags[j]: rank j's flag array of
- *   (m / 128) * ceil(n / 64) uint32, zeroed once at allocation.
- * epoch: a call counter identical on all ranks, never 0; consecutive calls
- * must alternate between two buffer sets (a rank may run one call ahead).
- * tile_n: 0 for the heuristic or a tm_scaled_mm_i8_tile configuration.
+ * The epilogue stores each bf16 partial 128-row block of owner j's rows into
+ * peer_part[j], slot `rank` (NVLink peer stores), while the GEMM runs; each
+ * CTA then drains its stores once and adds the number of elements it sent
+ * to owner j to peer_flags[j][rank].  CTAs without GEMM work left wait
+ * (bounded) until every source's counter shows all of this rank's blocks,
+ * sum them in rank order in fp32, add `bias` ([n] bf16 or NULL) once and
+ * write out[m / world, n] (row stride ldo).
+ * peer_part[j]: device pointer (local or IPC-mapped) to rank j's receive
+ *   buffer of world x (m / world) x n bf16; peer_flags[j]: rank j's array of
+ *   `world` uint64 counters, zeroed once at allocation and never reset.
+ * epoch: 1-based count of calls made with this buffer set, identical on all
+ * ranks; consecutive calls must alternate between two buffer sets (a rank may
+ * run one call ahead), and every call on a set must use the same m, n and
+ * world.  tile_n: 0 = heuristic, or a tm_scaled_mm_i8_tile configuration.
  * Waits that run out record a device status (tm_device_status).
  */
 int tm_scaled_mm_i8_reduce_scatter(void* out, const int8_t* a, const int8_t* b,

@@ -60,20 +60,21 @@ struct GemmArgs {
   int* status;
   // Row-parallel fused reduce-scatter; world == 0 disables it.  Rank j owns
   // rows [j * rows_per_owner, +rows_per_owner).  The epilogue stores each
-  // bf16 partial block of owner j's rows into peer_part[j], slot `rank`
-  // ([world][rows_per_owner][N], an NVLink peer store unless j == rank), and
-  // publishes `epoch` for the 128-row x tile-width block in peer_flags[j]
-  // ([world][rows_per_owner/128][num_n]).  CTAs that run out of GEMM tiles
-  // then reduce this rank's rows from its own slots (local HBM reads): wait
-  // for each source's block flag, sum in rank order, add red_bias, store to
-  // red_out.
+  // bf16 partial 128-row block of owner j's rows into peer_part[j], slot
+  // `rank` ([world][rows_per_owner][N], an NVLink peer store unless
+  // j == rank).  When a CTA has stored all its blocks it drains its stores
+  // once and adds the number of elements it sent to owner j to
+  // peer_count[j][rank] (a 64-bit counter that only grows).  CTAs that run
+  // out of GEMM tiles then wait until every source's counter reaches
+  // `uses` x rows_per_owner x N, and reduce this rank's rows from its own
+  // slots (local HBM reads): sum in rank order, add red_bias, store to red_out.
   int world, rank, rows_per_owner;
-  uint32_t epoch;
+  uint32_t uses;  // 1-based count of calls made with this buffer set
   const __nv_bfloat16* red_bias;
   __nv_bfloat16* red_out;
   int64_t red_ldo;
   __nv_bfloat16* peer_part[kMaxPeers];
-  uint32_t* peer_flags[kMaxPeers];
+  unsigned long long* peer_count[kMaxPeers];
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
@@ -266,16 +267,6 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tmem_b
   }
 }
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
 __device__ __forceinline__ uint4 ld_cg16(const void* p) {
   uint4 r;
   asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];"
@@ -284,28 +275,29 @@ __device__ __forceinline__ uint4 ld_cg16(const void* p) {
   return r;
 }
 
-// Fused reduce-scatter: once all 8 epilogue warps have issued the stores of
-// a 128-row block into its owner's slot, one thread publishes the block's
-// flag on the owner.  The named barrier orders every warp's stores before
-// that thread's system-scope fence and release store (fences are cumulative),
-// so only one thread waits for the stores to land.
-__device__ __forceinline__ void publish_block(const GemmArgs& g, int64_t row0, int nb, int warp,
-                                              int lane) {
+// Fused reduce-scatter: after a CTA's epilogue warps have issued the stores
+// of all their blocks, one thread drains them (the named barrier orders
+// every warp's stores before that thread's system-scope fence; fences are
+// cumulative) and adds the per-owner element counts to the owners' counters.
+// One drain per CTA instead of one per block keeps the NVLink stores
+// streaming while the GEMM runs.
+__device__ __forceinline__ void publish_counts(const GemmArgs& g, const int* sent, int warp,
+                                               int lane) {
   asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
   if (warp == 2 && lane == 0) {
-    const int owner = static_cast<int>(row0 / g.rows_per_owner);
-    const int lrb = static_cast<int>((row0 - static_cast<int64_t>(owner) * g.rows_per_owner) / kBM);
     __threadfence_system();
-    st_release_sys(g.peer_flags[owner] +
-                       (static_cast<int64_t>(g.rank) * (g.rows_per_owner / kBM) + lrb) * g.num_n +
-                       nb,
-                   g.epoch);
+    for (int j = 0; j < g.world; ++j)
+      if (sent[j] > 0)
+        asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(g.peer_count[j] + g.rank),
+                     "l"(static_cast<unsigned long long>(sent[j]))
+                     : "memory");
   }
 }
 
-// Flag values are call epochs; "reached" is a wrap-safe epoch comparison.
-__device__ __forceinline__ bool epoch_reached(uint32_t flag, uint32_t epoch) {
-  return static_cast<int32_t>(flag - epoch) >= 0;
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
 }
 
 // Sum one block's partials from `world` (<= W) source slots, V vectors of 8
@@ -376,35 +368,41 @@ __device__ __forceinline__ void reduce_block(const GemmArgs& g, int lrb, int col
 // Fused reduce-scatter, owner side, run by every thread of a CTA that has no
 // GEMM tiles left (all CTAs of the cooperative persistent grid are resident,
 // and peers run concurrently on their own GPUs, so every wait here is on work
-// that is already executing).  Block (row block, column tile) of this rank's
-// rows: wait for all sources' flags, read the bf16 partials the sources
-// pushed into this rank's slots (local HBM), sum in rank order in fp32, add
-// the bias, store.  Waits are bounded; a timeout records the device status
-// and skips the block.
+// that is already executing).  Wait until every source's counter shows all
+// of this rank's blocks have landed, then for each (row block, column tile)
+// read the bf16 partials the sources pushed into this rank's slots (local
+// HBM), sum in rank order in fp32, add the bias, store.  The wait is
+// bounded; a timeout records the device status and skips the reduction.
 __device__ void reduce_phase(const GemmArgs& g, int bn, int cta, int ctas) {
   const int rbpo = g.rows_per_owner / kBM;
   const int tiles = rbpo * g.num_n;
+  if (cta >= tiles) return;
+  // Every source sends each element of this rank's rows_per_owner x N block
+  // once per call; its counter reaches uses x rows_per_owner x N once all of
+  // them have landed (independent of the tile configuration).
+  const unsigned long long target = static_cast<unsigned long long>(g.uses) *
+                                    static_cast<unsigned long long>(g.rows_per_owner) *
+                                    static_cast<unsigned long long>(g.N);
+  int ok = 1;
+  if (threadIdx.x < static_cast<unsigned>(g.world)) {
+    const unsigned long long* c = g.peer_count[g.rank] + threadIdx.x;
+    bool seen = ld_acquire_sys_u64(c) >= target;
+    if (!seen) {
+      const uint64_t t0 = globaltimer_ns();
+      while (!(seen = ld_acquire_sys_u64(c) >= target)) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+        __nanosleep(64);
+      }
+    }
+    if (!seen) {
+      ok = 0;
+      if (g.status) atomicExch(g.status, kDevWaitTimeout);
+    }
+  }
+  if (!__syncthreads_and(ok)) return;
   for (int t = cta; t < tiles; t += ctas) {
     const int lrb = t / g.num_n;
     const int nb = t - lrb * g.num_n;
-    int ok = 1;
-    if (threadIdx.x < static_cast<unsigned>(g.world)) {
-      const uint32_t* f =
-          g.peer_flags[g.rank] + (static_cast<int64_t>(threadIdx.x) * rbpo + lrb) * g.num_n + nb;
-      bool seen = epoch_reached(ld_acquire_sys(f), g.epoch);
-      if (!seen) {
-        const uint64_t t0 = globaltimer_ns();
-        while (!(seen = epoch_reached(ld_acquire_sys(f), g.epoch))) {
-          if (globaltimer_ns() - t0 > kWaitLimitNs) break;
-          __nanosleep(32);
-        }
-      }
-      if (!seen) {
-        ok = 0;
-        if (g.status) atomicExch(g.status, kDevWaitTimeout);
-      }
-    }
-    if (!__syncthreads_and(ok)) continue;
     const int col0 = nb * bn;
     const int vec_per_row = min(bn, g.N - col0) / 8;
     if (g.world <= 2)
@@ -581,6 +579,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     int acc = 0;
     uint32_t acc_phase = 0;
+    int sent[kMaxPeers] = {};
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
       int mb, nb;
       tile_coords(tile, g.num_m, g.num_n, mb, nb);
@@ -593,12 +592,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar.tmem_empty[acc]);
       if (g.world > 0 && static_cast<int64_t>(mb) * kBM < g.M)
-        publish_block(g, static_cast<int64_t>(mb) * kBM, nb, warp, lane);
+        sent[static_cast<int>(static_cast<int64_t>(mb) * kBM / g.rows_per_owner)] +=
+            kBM * min(BN, g.N - nb * BN);
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
       }
     }
+    if (g.world > 0) publish_counts(g, sent, warp, lane);
   }
 
   tc_fence_before();
@@ -759,6 +760,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t empty_leader1 = map_to_cta(smem_u32(&bar.tmem_empty[1]), 0);
     int acc = 0;
     uint32_t acc_phase = 0;
+    int sent[kMaxPeers] = {};
     for (int tile = pair; tile < tiles; tile += pairs) {
       int mb, nb;
       tile_coords(tile, g.num_m, g.num_n, mb, nb);
@@ -770,12 +772,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc == 0 ? empty_leader0 : empty_leader1);
-      if (g.world > 0 && row0 < g.M) publish_block(g, row0, nb, warp, lane);
+      if (g.world > 0 && row0 < g.M)
+        sent[static_cast<int>(row0 / g.rows_per_owner)] += kBM * min(BN, g.N - nb * BN);
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
       }
     }
+    if (g.world > 0) publish_counts(g, sent, warp, lane);
   }
 
   tc_fence_before();
@@ -1015,13 +1019,13 @@ int scaled_mm_impl(void* out, int out_dtype, const int8_t* a, const int8_t* b, c
     args.world = scatter->world;
     args.rank = scatter->rank;
     args.rows_per_owner = static_cast<int>(m / scatter->world);
-    args.epoch = scatter->epoch;
+    args.uses = scatter->epoch;
     args.red_bias = static_cast<const __nv_bfloat16*>(bias);
     args.red_out = static_cast<__nv_bfloat16*>(out);
     args.red_ldo = ldo;
     for (int j = 0; j < scatter->world; ++j) {
       args.peer_part[j] = static_cast<__nv_bfloat16*>(scatter->peer_part[j]);
-      args.peer_flags[j] = static_cast<uint32_t*>(scatter->peer_flags[j]);
+      args.peer_count[j] = static_cast<unsigned long long*>(scatter->peer_flags[j]);
     }
   }
   const int max_pairs = max_resident_pairs(dev, sms);

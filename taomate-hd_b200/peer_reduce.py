@@ -4,21 +4,22 @@ The row-parallel linears of the reference sum their partial outputs with an
 NCCL all-reduce after the GEMM (src/taomate_hd/distributed/linear.py:279-289,
 collectives.py:19-40).  ``PeerReduceScatter`` runs the reduction inside the
 scaled-GEMM kernel instead (``tm_scaled_mm_i8_reduce_scatter`` in
-``include/taomate_w8a8.h``): each rank writes its bf16 partial blocks to its
-own buffer and flags them; CTAs that finished their GEMM tiles pull this
-rank's rows from every rank's buffer over NVLink, sum and add the bias, so
-the transfer overlaps the GEMM's tail.
+``include/taomate_w8a8.h``): the epilogue pushes each bf16 partial block to
+the rank that owns those rows over NVLink while the GEMM keeps running;
+each CTA then drains its stores once and bumps per-source counters on the
+owners; CTAs out of GEMM tiles wait for the counters and reduce their own
+rows from local memory.
 
-Each rank allocates one buffer holding two sets (alternate calls) of an
-``rows x cols`` bf16 partial plus its block flags, shares it by CUDA IPC
-handle over the TP process group, and maps every peer's buffer once.  All
-ranks must call in the same order with the same shapes; the call counter
-(epoch) is kept identically on every rank.
+Each rank allocates one buffer holding two sets (alternate calls) of
+``world`` receive slots (``rows x cols`` bf16 in total) plus ``world``
+64-bit counters, shares it by CUDA IPC handle over the TP process group,
+and maps every peer's buffer once.  All ranks must call in the same order
+with the same shapes and tile configuration; the per-set use counts are
+kept identically on every rank.
 """
 from __future__ import annotations
 
 import ctypes
-import math
 
 import torch
 
@@ -46,8 +47,8 @@ class PeerReduceScatter:
         self.rows_per_owner = rows // world
         self._lib = _native.capi()
         part_bytes = _align(rows * cols * 2)
-        flag_bytes = _align((rows // 128) * math.ceil(cols / 64) * 4)
-        self._half = part_bytes + flag_bytes
+        count_bytes = _align(world * 8)
+        self._half = part_bytes + count_bytes
         handle_size = self._lib.tm_peer_handle_size()
         handle = (ctypes.c_char * handle_size)()
         base = ctypes.c_void_p()
@@ -79,8 +80,9 @@ class PeerReduceScatter:
             torch.distributed.barrier(group=ctx.tp_group)
         arr = ctypes.c_void_p * world
         self._part = [arr(*[b + h * self._half for b in bases]) for h in (0, 1)]
-        self._flags = [arr(*[b + h * self._half + part_bytes for b in bases]) for h in (0, 1)]
-        self.epoch = 0
+        self._counts = [arr(*[b + h * self._half + part_bytes for b in bases]) for h in (0, 1)]
+        self.calls = 0
+        self._uses = [0, 0]
 
     def __call__(self, q: torch.Tensor, q_scale: torch.Tensor, w_q: torch.Tensor,
                  w_scale: torch.Tensor, bias: torch.Tensor | None, out: torch.Tensor,
@@ -96,14 +98,15 @@ class PeerReduceScatter:
             raise ValueError("shape differs from the one the buffers were built for")
         if out.shape != (self.rows_per_owner, self.cols) or out.dtype != torch.bfloat16:
             raise ValueError(f"out must be bf16 [{self.rows_per_owner}, {self.cols}]")
-        self.epoch += 1
-        half = self.epoch & 1
+        self.calls += 1
+        half = self.calls & 1
+        self._uses[half] += 1
         stream = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
         rc = self._lib.tm_scaled_mm_i8_reduce_scatter(
             out.data_ptr(), q.data_ptr(), w_q.data_ptr(), q_scale.data_ptr(), q_scale.numel(),
             w_scale.data_ptr(), w_scale.numel(), None if bias is None else bias.data_ptr(),
             m, self.cols, k, q.stride(0), w_q.stride(0), out.stride(0),
-            self._part[half], self._flags[half], self.world, self.rank, self.epoch & 0xFFFFFFFF,
+            self._part[half], self._counts[half], self.world, self.rank, self._uses[half],
             tile_n, stream)
         if rc != 0:
             raise RuntimeError(
