@@ -281,7 +281,7 @@ __device__ __forceinline__ uint4 ld_cg16(const void* p) {
 // cumulative) and adds the per-owner element counts to the owners' counters.
 // One drain per CTA instead of one per block keeps the NVLink stores
 // streaming while the GEMM runs.
-__device__ __forceinline__ void publish_counts(const GemmArgs& g, const int* sent, int warp,
+__device__ __forceinline__ void publish_counts(const GemmArgs& g, const long long* sent, int warp,
                                                int lane) {
   asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
   if (warp == 2 && lane == 0) {
@@ -579,7 +579,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     int acc = 0;
     uint32_t acc_phase = 0;
-    int sent[kMaxPeers] = {};
+    long long sent[kMaxPeers] = {};
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
       int mb, nb;
       tile_coords(tile, g.num_m, g.num_n, mb, nb);
@@ -760,7 +760,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t empty_leader1 = map_to_cta(smem_u32(&bar.tmem_empty[1]), 0);
     int acc = 0;
     uint32_t acc_phase = 0;
-    int sent[kMaxPeers] = {};
+    long long sent[kMaxPeers] = {};
     for (int tile = pair; tile < tiles; tile += pairs) {
       int mb, nb;
       tile_coords(tile, g.num_m, g.num_n, mb, nb);
