@@ -138,6 +138,36 @@ int tm_scaled_mm_i8_tile(void* out, int out_dtype, const int8_t* a, const int8_t
                          int32_t* acc_debug, int tile_n, void* stream);
 
 /*
+ * Split-K for skinny M.  tm_scaled_mm_i8_ws is tm_scaled_mm_i8_ex plus a
+ * caller-provided workspace; when the shape leaves most SMs idle (small M)
+ * it cuts K into slices computed by separate CTAs, which store exact int32
+ * partials in the workspace; the last slice of each tile to finish sums them
+ * and runs the epilogue (results are identical to the unsplit GEMM).  The
+ * workspace must be 16-byte aligned and zeroed before its first use; every
+ * complete call leaves its counters at zero again.  Calls that share a
+ * workspace must not overlap on the GPU.  With workspace_bytes smaller than
+ * tm_scaled_mm_i8_workspace_size(m, n, k) the call runs unsplit.
+ * tm_scaled_mm_i8_splitk forces a one-CTA tile width (256/128/64) and a
+ * slice count (for tests); tm_scaled_mm_i8_splitk_workspace_size gives its
+ * workspace bytes.  Same reference counterpart as tm_cutlass_scaled_mm.
+ */
+int tm_scaled_mm_i8_workspace_size(int64_t m, int64_t n, int64_t k, uint64_t* bytes);
+int tm_scaled_mm_i8_ws(void* out, int out_dtype, const int8_t* a, const int8_t* b,
+                       const float* scale_a, int64_t scale_a_numel, const float* scale_b,
+                       int64_t scale_b_numel, const void* bias, int64_t m, int64_t n,
+                       int64_t k, int64_t lda, int64_t ldb, int64_t ldo, uint32_t epilogue,
+                       int32_t* acc_debug, void* workspace, uint64_t workspace_bytes,
+                       void* stream);
+int tm_scaled_mm_i8_splitk(void* out, int out_dtype, const int8_t* a, const int8_t* b,
+                           const float* scale_a, int64_t scale_a_numel, const float* scale_b,
+                           int64_t scale_b_numel, const void* bias, int64_t m, int64_t n,
+                           int64_t k, int64_t lda, int64_t ldb, int64_t ldo, uint32_t epilogue,
+                           int32_t* acc_debug, int tile_n, int splits, void* workspace,
+                           uint64_t workspace_bytes, void* stream);
+int tm_scaled_mm_i8_splitk_workspace_size(int64_t m, int64_t n, int64_t k, int tile_n,
+                                          int splits, uint64_t* bytes);
+
+/*
  * Row-parallel scaled GEMM with the reduce-scatter fused into the kernel
  * (the row-parallel fc2 / out-projection; the reference's
  * RowParallelLinear.forward = forward_local + tp all-reduce + bias,

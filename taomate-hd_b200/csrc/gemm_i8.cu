@@ -58,6 +58,14 @@ struct GemmArgs {
   int num_m, num_n, kblocks;  // tile grid (in units of the kernel's tile)
   uint32_t epilogue;
   int* status;
+  // Split-K (one-CTA kernel): each tile's K range is cut into `splits`
+  // slices of kb_per_split k-blocks; every (tile, slice) unit stores its exact
+  // int32 partial in ws[slice][M][N] and bumps tile_counters[tile]; the unit
+  // that arrives last sums the slices, runs the epilogue and resets the
+  // counter to 0.  splits == 1 disables it.
+  int splits, kb_per_split;
+  int32_t* ws;
+  unsigned int* tile_counters;
   // Row-parallel fused reduce-scatter; world == 0 disables it.  Rank j owns
   // rows [j * rows_per_owner, +rows_per_owner).  The epilogue stores each
   // bf16 partial 128-row block of owner j's rows into peer_part[j], slot
@@ -414,6 +422,116 @@ __device__ void reduce_phase(const GemmArgs& g, int bn, int cta, int ctas) {
   }
 }
 
+// Write a staged 32-row x (chunks x 16 bytes) block back as row segments:
+// `chunks` lanes cover one row, 32 / chunks rows per store instruction.
+template <typename OutT>
+__device__ __forceinline__ void write_staged(const GemmArgs& g, uint8_t* stage, int64_t row_base,
+                                             int col0, int chunks, int lane) {
+  const int rows_per_store = 32 / chunks;
+  const int chunk = lane % chunks;
+  const int col = col0 + chunk * (16 / static_cast<int>(sizeof(OutT)));
+#pragma unroll 1
+  for (int rr = lane / chunks; rr < 32; rr += rows_per_store) {
+    const int64_t out_r = row_base + rr;
+    if (out_r < g.M && col < g.N)
+      *reinterpret_cast<uint4*>(out_row_ptr<OutT>(g, out_r) + col) = *stage_slot(stage, rr, chunk);
+  }
+}
+
+// Split-K epilogue of one epilogue warp for one (tile, slice) unit:
+//  1. store this slice's int32 partial (lane quarter warp % 4, column half
+//     (warp-2)/4) to ws[slice] as 128-byte row segments;
+//  2. count the unit on the tile; the unit that arrives last
+//  3. sums every slice's partial (exact int32) and runs the usual
+//     dequant / bias / GELU epilogue on the sum.
+template <int BN, typename OutT>
+__device__ __forceinline__ void splitk_epilogue(const GemmArgs& g, uint32_t tmem_base,
+                                                uint32_t acc_col, int64_t row0, int col0,
+                                                int tile, int slice, int warp, int lane,
+                                                uint8_t* stage, volatile int* last_flag) {
+  constexpr int kHalf = BN / 2;
+  const int q = warp & 3;
+  const int h = (warp - 2) >> 2;
+  const int64_t row_base = row0 + q * 32;
+  const int64_t row = row_base + lane;
+  const int64_t slice_elems = static_cast<int64_t>(g.M) * g.N;
+  const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc_col +
+                         static_cast<uint32_t>(h * kHalf);
+#pragma unroll 1
+  for (int c = 0; c < kHalf / 32; ++c) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c * 32), r);
+    tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      *stage_slot(stage, lane, j) = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+    __syncwarp();
+    const int col_c = col0 + h * kHalf + c * 32;
+    const int chunk = lane % 8;
+    const int col = col_c + chunk * 4;
+#pragma unroll 1
+    for (int rr = lane / 8; rr < 32; rr += 4) {
+      const int64_t out_r = row_base + rr;
+      if (out_r < g.M && col < g.N)
+        *reinterpret_cast<uint4*>(g.ws + slice * slice_elems + out_r * g.N + col) =
+            *stage_slot(stage, rr, chunk);
+    }
+    __syncwarp();
+  }
+  __threadfence();
+  asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
+  if (warp == 2 && lane == 0) {
+    const unsigned int prior = atomicAdd(g.tile_counters + tile, 1u);
+    const int last = prior == static_cast<unsigned int>(g.splits - 1);
+    if (last) g.tile_counters[tile] = 0u;  // every slice has arrived: reset for the next call
+    *last_flag = last;
+  }
+  asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
+  if (!*last_flag) return;
+  __threadfence();
+  const bool row_ok = row < g.M;
+  const float sa = row_ok ? (g.sa_per_row ? __ldg(g.sa + row) : __ldg(g.sa)) : 0.f;
+  int32_t* dbg_row = (g.acc_debug != nullptr && row_ok)
+                         ? g.acc_debug + row * static_cast<int64_t>(g.N) : nullptr;
+#pragma unroll 1
+  for (int c = 0; c < kHalf / 32; ++c) {
+    const int col = col0 + h * kHalf + c * 32;
+    uint32_t sum[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) sum[j] = 0u;
+    if (row_ok) {
+      for (int sl = 0; sl < g.splits; ++sl) {
+        const int32_t* src = g.ws + sl * slice_elems + row * g.N + col;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (col + 4 * j < g.N) {
+            const uint4 v = ld_cg16(src + 4 * j);
+            sum[4 * j] += v.x;
+            sum[4 * j + 1] += v.y;
+            sum[4 * j + 2] += v.z;
+            sum[4 * j + 3] += v.w;
+          }
+        }
+      }
+    }
+    uint4 o[4];
+    epilogue16<OutT>(g, sum, sa, col, o[0], o[1]);
+    epilogue16<OutT>(g, sum + 16, sa, col + 16, o[2], o[3]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) *stage_slot(stage, lane, j) = o[j];
+    if (dbg_row != nullptr) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4)
+        if (col + j < g.N)
+          *reinterpret_cast<uint4*>(dbg_row + col + j) =
+              make_uint4(sum[j], sum[j + 1], sum[j + 2], sum[j + 3]);
+    }
+    __syncwarp();
+    write_staged<OutT>(g, stage, row_base, col, 32 * static_cast<int>(sizeof(OutT)) / 16, lane);
+    __syncwarp();
+  }
+}
+
 template <int BN_CTA, int STAGES>
 struct Smem {
   static constexpr int kABytes = kBM * kBK;
@@ -434,6 +552,7 @@ struct Barriers {
   uint64_t* tmem_empty;
   uint32_t* tmem_slot;
   volatile int* abort_flag;
+  volatile int* split_last;  // split-K: "this CTA completes the tile"
 };
 
 template <int STAGES>
@@ -445,6 +564,7 @@ __device__ __forceinline__ Barriers carve_barriers(uint8_t* base) {
   b.tmem_empty = b.tmem_full + 2;
   b.tmem_slot = reinterpret_cast<uint32_t*>(b.tmem_empty + 2);
   b.abort_flag = reinterpret_cast<volatile int*>(b.tmem_slot + 1);
+  b.split_last = reinterpret_cast<volatile int*>(b.tmem_slot + 2);
   return b;
 }
 
@@ -467,7 +587,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int tiles = g.num_m * g.num_n;
+  const int units = g.num_m * g.num_n * g.splits;  // (tile, K slice) work units
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -500,10 +620,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       uint32_t issued_mask = 0, issued_parity = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
+      for (int unit = blockIdx.x; ok && unit < units; unit += gridDim.x) {
+        const int tile = unit / g.splits;
+        const int kb0 = (unit - tile * g.splits) * g.kb_per_split;
+        const int kb1 = min(kb0 + g.kb_per_split, g.kblocks);
         int mb, nb;
         tile_coords(tile, g.num_m, g.num_n, mb, nb);
-        for (int kb = 0; kb < g.kblocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&bar.empty[stage], phase ^ 1u, bar.abort_flag, g.status)) {
             ok = false;
             break;
@@ -535,14 +658,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true, issued_any = false;
-      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
+      for (int unit = blockIdx.x; ok && unit < units; unit += gridDim.x) {
+        const int tile = unit / g.splits;
+        const int kb0 = (unit - tile * g.splits) * g.kb_per_split;
+        const int kb1 = min(kb0 + g.kb_per_split, g.kblocks);
         if (!mbar_wait(&bar.tmem_empty[acc], acc_phase ^ 1u, bar.abort_flag, g.status)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < g.kblocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&bar.full[stage], phase, bar.abort_flag, g.status)) {
             ok = false;
             break;
@@ -553,7 +679,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int k = 0; k < kBK / 32; ++k)
             umma_i8(d_tmem, make_desc_kmajor_sw128(a_addr + k * 32),
-                    make_desc_kmajor_sw128(b_addr + k * 32), kIdesc, (kb | k) != 0 ? 1u : 0u);
+                    make_desc_kmajor_sw128(b_addr + k * 32), kIdesc,
+                    ((kb - kb0) | k) != 0 ? 1u : 0u);
           issued_any = true;
           umma_commit(&bar.empty[stage]);
           if (++stage == STAGES) {
@@ -580,14 +707,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     long long sent[kMaxPeers] = {};
-    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    for (int unit = blockIdx.x; unit < units; unit += gridDim.x) {
+      const int tile = unit / g.splits;
       int mb, nb;
       tile_coords(tile, g.num_m, g.num_n, mb, nb);
       if (!mbar_wait(&bar.tmem_full[acc], acc_phase, bar.abort_flag, g.status)) break;
       tc_fence_after();
-      epilogue_tile<BN, OutT>(g, tmem_base, static_cast<uint32_t>(acc * BN),
-                              static_cast<int64_t>(mb) * kBM, nb * BN, warp, lane,
-                              smem + L::kEpiOffset + (warp - 2) * kEpiStageBytes);
+      uint8_t* stage = smem + L::kEpiOffset + (warp - 2) * kEpiStageBytes;
+      if (g.splits > 1)
+        splitk_epilogue<BN, OutT>(g, tmem_base, static_cast<uint32_t>(acc * BN),
+                                  static_cast<int64_t>(mb) * kBM, nb * BN, tile,
+                                  unit - tile * g.splits, warp, lane, stage, bar.split_last);
+      else
+        epilogue_tile<BN, OutT>(g, tmem_base, static_cast<uint32_t>(acc * BN),
+                                static_cast<int64_t>(mb) * kBM, nb * BN, warp, lane, stage);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar.tmem_empty[acc]);
@@ -814,9 +947,9 @@ int launch_single(const Operands& op, GemmArgs args, int sms, cudaStream_t strea
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal) !=
       cudaSuccess)
     return TM_ERR_CUDA;
-  const int tiles = args.num_m * args.num_n;
+  const int units = args.num_m * args.num_n * args.splits;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(tiles < sms ? tiles : sms));
+  cfg.gridDim = dim3(static_cast<unsigned>(units < sms ? units : sms));
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = L::kTotal;
   cfg.stream = stream;
@@ -886,13 +1019,13 @@ int dispatch(const Operands& op, const GemmArgs& args, int cfg, int sms, int max
   }
 }
 
-// Relative time of a configuration: waves of tiles over the resident CTAs
-// (or pairs) times the per-SM work of one tile (proportional to its N width)
-// divided by that configuration's sustained efficiency.  The efficiencies
-// are B200 measurements at M=20480, N=9216, K=3072 (normalised to the
-// 256-wide pair tile): narrower tiles need more operand bytes per MMA and
-// fall further below the tensor rate.
-double estimate(int cfg, int m, int n, int sms, int max_pairs) {
+// Relative time of an unsplit configuration: waves of tiles over the
+// resident CTAs (or pairs) times the per-SM length of one tile -- its
+// k-blocks (plus ~2 for filling the pipeline) times its N width, divided by
+// that configuration's sustained efficiency.  The efficiencies are B200
+// measurements at M=20480, N=9216, K=3072 (normalised to the 256-wide pair
+// tile): narrower tiles need more operand bytes per MMA.
+double estimate(int cfg, int m, int n, int kblocks, int sms, int max_pairs) {
   const bool pair = cfg > kPairFlag;
   const int bn = pair ? cfg - kPairFlag : cfg;
   double eff;
@@ -907,23 +1040,70 @@ double estimate(int cfg, int m, int n, int sms, int max_pairs) {
   const double rows = pair ? 2.0 * kBM : kBM;
   const double tiles = std::ceil(m / rows) * std::ceil(static_cast<double>(n) / bn);
   const double slots = pair ? max_pairs : sms;
-  const double waves = std::ceil(tiles / slots);
-  return waves * bn / eff;
+  return std::ceil(tiles / slots) * (kblocks + 2.0) * bn / eff;
 }
 
-int pick_config(int m, int n, int sms, int max_pairs) {
+struct Choice {
+  int cfg;
+  int splits;
+};
+
+// Best (configuration, K slices).  Split-K (one-CTA kernel, 64-wide tiles)
+// pays only when K is long and the tile grid leaves most SMs idle: on B200 a
+// (tile, slice) unit has a fixed cost of several microseconds (pipeline fill,
+// the int32 partial round trip through L2), so at K = 3072 splitting never
+// won, while at K = 12288 and M <= 256 it cut the time by 1.4-2x (3-6
+// slices).  Rule: K >= 48 k-blocks and at most half the SMs covered by the
+// unsplit 64-wide grid; slices = as many as keep one wave of units and at
+// least 16 k-blocks per slice, up to 8.
+Choice pick_choice(int m, int n, int kblocks, int sms, int max_pairs, bool allow_split) {
+  if (allow_split && kblocks >= 48) {
+    const int tiles64 = ((m + kBM - 1) / kBM) * ((n + 63) / 64);
+    if (2 * tiles64 <= sms) {
+      int splits = sms / tiles64;
+      splits = min(splits, kblocks / 16);
+      splits = min(splits, 8);
+      if (splits >= 2) return Choice{64, splits};
+    }
+  }
   static const int kConfigs[] = {kPairFlag + 256, kPairFlag + 192, kPairFlag + 128, 256, 128, 64};
-  int best = 256;
+  Choice best{256, 1};
   double best_t = -1.0;
   for (int cfg : kConfigs) {
     if (cfg > kPairFlag && max_pairs <= 0) continue;
-    const double t = estimate(cfg, m, n, sms, max_pairs);
+    const double t = estimate(cfg, m, n, kblocks, sms, max_pairs);
     if (best_t < 0 || t < best_t) {
       best_t = t;
-      best = cfg;
+      best = Choice{cfg, 1};
     }
   }
   return best;
+}
+
+// Effective slice count (no empty slice) and workspace bytes of a split-K
+// run: per-tile counters (256-byte aligned) followed by `splits` int32 [M, N].
+struct SplitPlan {
+  int splits;
+  int kb_per_split;
+  uint64_t counter_bytes;
+  uint64_t bytes;
+};
+
+SplitPlan plan_split(int cfg, int splits, int m, int n, int kblocks) {
+  SplitPlan p{1, kblocks, 0, 0};
+  if (splits <= 1 || cfg > kPairFlag) return p;
+  const int bn = cfg;
+  p.kb_per_split = (kblocks + splits - 1) / splits;
+  p.splits = (kblocks + p.kb_per_split - 1) / p.kb_per_split;
+  if (p.splits <= 1) {
+    p.splits = 1;
+    p.kb_per_split = kblocks;
+    return p;
+  }
+  const uint64_t tiles = static_cast<uint64_t>((m + kBM - 1) / kBM) * ((n + bn - 1) / bn);
+  p.counter_bytes = (tiles * 4 + 255) / 256 * 256;
+  p.bytes = p.counter_bytes + static_cast<uint64_t>(p.splits) * m * n * 4;
+  return p;
 }
 
 // Resident CTA pairs of the pair kernel on a device (cached per device).
@@ -965,11 +1145,19 @@ struct ScatterSpec {
   uint32_t epoch;
 };
 
+// Optional split-K workspace (zeroed by the caller before its first use; the
+// kernel leaves its counters at zero again after every complete call).
+struct Workspace {
+  void* ptr;
+  uint64_t bytes;
+  int force_splits;  // 0 = heuristic
+};
+
 int scaled_mm_impl(void* out, int out_dtype, const int8_t* a, const int8_t* b, const float* sa,
                    int64_t sa_numel, const float* sb, int64_t sb_numel, const void* bias,
                    int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldo,
                    uint32_t epilogue, int32_t* acc_debug, int force_cfg, cudaStream_t stream,
-                   const ScatterSpec* scatter = nullptr) {
+                   const ScatterSpec* scatter = nullptr, const Workspace* ws = nullptr) {
   if (out_dtype != TM_DTYPE_BF16 && out_dtype != TM_DTYPE_FP16) return TM_ERR_DTYPE;
   if (m < 0 || n <= 0 || k <= 0) return TM_ERR_SHAPE;
   if (m > 0x7fffffffLL || n > 0x7fffffffLL || k > 0x7fffffffLL) return TM_ERR_TOO_LARGE;
@@ -1029,8 +1217,29 @@ int scaled_mm_impl(void* out, int out_dtype, const int8_t* a, const int8_t* b, c
     }
   }
   const int max_pairs = max_resident_pairs(dev, sms);
-  const int cfg = force_cfg ? force_cfg : pick_config(args.M, args.N, sms, max_pairs);
+  const bool can_split = ws != nullptr && ws->ptr != nullptr && scatter == nullptr;
+  Choice choice = pick_choice(args.M, args.N, args.kblocks, sms, max_pairs, can_split);
+  if (force_cfg) choice = Choice{force_cfg, 1};
+  if (can_split && ws->force_splits > 0) choice.splits = ws->force_splits;
+  const int cfg = choice.cfg;
   if (cfg > kPairFlag && max_pairs <= 0) return TM_ERR_UNSUPPORTED;
+  args.splits = 1;
+  args.kb_per_split = args.kblocks;
+  if (can_split && choice.splits > 1 && cfg < kPairFlag) {
+    const SplitPlan plan = plan_split(cfg, choice.splits, args.M, args.N, args.kblocks);
+    if (plan.splits > 1) {
+      if (plan.bytes > ws->bytes) {
+        if (ws->force_splits > 0) return TM_ERR_TOO_LARGE;  // forced split needs the space
+      } else if (!aligned16(ws->ptr)) {
+        return TM_ERR_ALIGNMENT;
+      } else {
+        args.splits = plan.splits;
+        args.kb_per_split = plan.kb_per_split;
+        args.tile_counters = static_cast<unsigned int*>(ws->ptr);
+        args.ws = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(ws->ptr) + plan.counter_bytes);
+      }
+    }
+  }
   const Operands op{a, lda, b, ldb};
   if (out_dtype == TM_DTYPE_BF16)
     return dispatch<__nv_bfloat16>(op, args, cfg, sms, max_pairs, stream);
@@ -1070,6 +1279,60 @@ int tm_scaled_mm_i8_reduce_scatter(void* out, const int8_t* a, const int8_t* b,
   return tmw::scaled_mm_impl(out, TM_DTYPE_BF16, a, b, scale_a, scale_a_numel, scale_b,
                              scale_b_numel, bias, m, n, k, lda, ldb, ldo, 0u, nullptr, tile_n,
                              tmw::as_stream(stream), &spec);
+}
+
+int tm_scaled_mm_i8_workspace_size(int64_t m, int64_t n, int64_t k, uint64_t* bytes) {
+  if (bytes == nullptr) return TM_ERR_NULL_POINTER;
+  *bytes = 0;
+  if (m < 0 || n <= 0 || k <= 0) return TM_ERR_SHAPE;
+  if (m == 0) return TM_OK;
+  if (m > 0x7fffffffLL || n > 0x7fffffffLL || k > 0x7fffffffLL) return TM_ERR_TOO_LARGE;
+  const int dev = tmw::current_device();
+  const int sms = tmw::sm_count(dev);
+  if (sms <= 0) return TM_ERR_CUDA;
+  const int kblocks = static_cast<int>((k + tmw::kBK - 1) / tmw::kBK);
+  const int max_pairs = tmw::max_resident_pairs(dev, sms);
+  const tmw::Choice c = tmw::pick_choice(static_cast<int>(m), static_cast<int>(n), kblocks, sms,
+                                         max_pairs, true);
+  *bytes = tmw::plan_split(c.cfg, c.splits, static_cast<int>(m), static_cast<int>(n), kblocks).bytes;
+  return TM_OK;
+}
+
+int tm_scaled_mm_i8_ws(void* out, int out_dtype, const int8_t* a, const int8_t* b,
+                       const float* scale_a, int64_t scale_a_numel, const float* scale_b,
+                       int64_t scale_b_numel, const void* bias, int64_t m, int64_t n, int64_t k,
+                       int64_t lda, int64_t ldb, int64_t ldo, uint32_t epilogue,
+                       int32_t* acc_debug, void* workspace, uint64_t workspace_bytes,
+                       void* stream) {
+  const tmw::Workspace ws{workspace, workspace_bytes, 0};
+  return tmw::scaled_mm_impl(out, out_dtype, a, b, scale_a, scale_a_numel, scale_b, scale_b_numel,
+                             bias, m, n, k, lda, ldb, ldo, epilogue, acc_debug, 0,
+                             tmw::as_stream(stream), nullptr, &ws);
+}
+
+int tm_scaled_mm_i8_splitk(void* out, int out_dtype, const int8_t* a, const int8_t* b,
+                           const float* scale_a, int64_t scale_a_numel, const float* scale_b,
+                           int64_t scale_b_numel, const void* bias, int64_t m, int64_t n,
+                           int64_t k, int64_t lda, int64_t ldb, int64_t ldo, uint32_t epilogue,
+                           int32_t* acc_debug, int tile_n, int splits, void* workspace,
+                           uint64_t workspace_bytes, void* stream) {
+  if (tile_n != 256 && tile_n != 128 && tile_n != 64) return TM_ERR_UNSUPPORTED;
+  if (splits < 1 || splits > 64) return TM_ERR_UNSUPPORTED;
+  if (workspace == nullptr) return TM_ERR_NULL_POINTER;
+  const tmw::Workspace ws{workspace, workspace_bytes, splits};
+  return tmw::scaled_mm_impl(out, out_dtype, a, b, scale_a, scale_a_numel, scale_b, scale_b_numel,
+                             bias, m, n, k, lda, ldb, ldo, epilogue, acc_debug, tile_n,
+                             tmw::as_stream(stream), nullptr, &ws);
+}
+
+int tm_scaled_mm_i8_splitk_workspace_size(int64_t m, int64_t n, int64_t k, int tile_n,
+                                          int splits, uint64_t* bytes) {
+  if (bytes == nullptr) return TM_ERR_NULL_POINTER;
+  if (tile_n != 256 && tile_n != 128 && tile_n != 64) return TM_ERR_UNSUPPORTED;
+  if (m <= 0 || n <= 0 || k <= 0) return TM_ERR_SHAPE;
+  const int kblocks = static_cast<int>((k + tmw::kBK - 1) / tmw::kBK);
+  *bytes = tmw::plan_split(tile_n, splits, static_cast<int>(m), static_cast<int>(n), kblocks).bytes;
+  return TM_OK;
 }
 
 int tm_scaled_mm_i8_tile(void* out, int out_dtype, const int8_t* a, const int8_t* b,

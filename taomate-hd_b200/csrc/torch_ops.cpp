@@ -5,10 +5,17 @@
 // (src/taomate_hd/inference/w8a8.py:22-35, :71-72).  Only a CUDA kernel is
 // registered: CPU tensors raise (no CPU fallback).  Every op validates
 // dtype/device/layout with TORCH_CHECK (RuntimeError in Python), launches on
-// the current CUDA stream and never allocates.
+// the current CUDA stream.  The only allocation is the split-K workspace of
+// cutlass_scaled_mm / scaled_mm_i8_ex (cached per device and stream, from
+// torch's caching allocator) for shapes that use split-K.
 #include <ATen/cuda/CUDAContext.h>
+#include <ATen/ops/zeros.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/library.h>
+
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "../../include/taomate_w8a8.h"
 
@@ -94,6 +101,24 @@ void static_scaled_int8_quant(at::Tensor& out, const at::Tensor& input, const at
                "static_scaled_int8_quant");
 }
 
+// Split-K workspace per (device, stream): zeroed when allocated, grown on
+// demand, reused by every call on that stream (calls on one stream never
+// overlap).  The kernels leave its counters at zero after each call.
+at::Tensor splitk_workspace(const at::Tensor& like, uint64_t bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<int, cudaStream_t>, at::Tensor> cache;
+  const cudaStream_t stream = at::cuda::getCurrentCUDAStream(like.device().index()).stream();
+  const std::pair<int, cudaStream_t> key{like.device().index(), stream};
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it == cache.end() || static_cast<uint64_t>(it->second.numel()) < bytes) {
+    at::Tensor ws = at::zeros({static_cast<int64_t>(bytes)}, like.options().dtype(at::kByte));
+    cache[key] = ws;
+    return ws;
+  }
+  return it->second;
+}
+
 void scaled_mm_common(at::Tensor& out, const at::Tensor& a, const at::Tensor& b,
                       const at::Tensor& a_scales, const at::Tensor& b_scales,
                       const std::optional<at::Tensor>& bias, int64_t epilogue,
@@ -148,11 +173,23 @@ void scaled_mm_common(at::Tensor& out, const at::Tensor& a, const at::Tensor& b,
                                   static_cast<uint32_t>(epilogue), acc_ptr,
                                   static_cast<int>(tile_n), stream_of(a));
   } else {
-    status = tm_scaled_mm_i8_ex(out.data_ptr(), out_dt, a.data_ptr<int8_t>(), b.data_ptr<int8_t>(),
-                                a_scales.data_ptr<float>(), a_scales.numel(),
-                                b_scales.data_ptr<float>(), b_scales.numel(), bias_ptr, m, n, k,
-                                lda, ldb, ldo, static_cast<uint32_t>(epilogue), acc_ptr,
-                                stream_of(a));
+    uint64_t ws_bytes = 0;
+    status = m > 0 ? tm_scaled_mm_i8_workspace_size(m, n, k, &ws_bytes) : TM_OK;
+    if (status == TM_OK && ws_bytes > 0) {
+      at::Tensor ws = splitk_workspace(a, ws_bytes);
+      status = tm_scaled_mm_i8_ws(out.data_ptr(), out_dt, a.data_ptr<int8_t>(),
+                                  b.data_ptr<int8_t>(), a_scales.data_ptr<float>(),
+                                  a_scales.numel(), b_scales.data_ptr<float>(), b_scales.numel(),
+                                  bias_ptr, m, n, k, lda, ldb, ldo,
+                                  static_cast<uint32_t>(epilogue), acc_ptr, ws.data_ptr(),
+                                  static_cast<uint64_t>(ws.numel()), stream_of(a));
+    } else if (status == TM_OK) {
+      status = tm_scaled_mm_i8_ex(out.data_ptr(), out_dt, a.data_ptr<int8_t>(),
+                                  b.data_ptr<int8_t>(), a_scales.data_ptr<float>(),
+                                  a_scales.numel(), b_scales.data_ptr<float>(), b_scales.numel(),
+                                  bias_ptr, m, n, k, lda, ldb, ldo,
+                                  static_cast<uint32_t>(epilogue), acc_ptr, stream_of(a));
+    }
   }
   check_status(status, op);
 }

@@ -133,3 +133,62 @@ def test_empty_m(tm_ops, cuda):
     y = tm_ops.cutlass_scaled_mm(a, b.t(), torch.ones(1, device=cuda), torch.ones(1, device=cuda),
                                  torch.bfloat16)
     assert y.shape == (0, 32)
+
+
+def _splitk_call(capi, cuda, a, b, sa, sb, bias, tile_n, splits, ws):
+    m, k = a.shape
+    n = b.shape[0]
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=cuda)
+    acc = torch.empty(m, n, dtype=torch.int32, device=cuda)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    rc = capi.tm_scaled_mm_i8_splitk(
+        out.data_ptr(), 0, a.data_ptr(), b.data_ptr(), sa.data_ptr(), sa.numel(), sb.data_ptr(),
+        sb.numel(), None if bias is None else bias.data_ptr(), m, n, k, k, k, n, 0, acc.data_ptr(),
+        tile_n, splits, ws.data_ptr(), ws.numel(), stream)
+    assert rc == 0, capi.tm_status_string(rc)
+    torch.cuda.synchronize()
+    return out.cpu(), acc.cpu().numpy()
+
+
+@pytest.mark.parametrize("tile_n,splits", [(64, 3), (128, 2), (256, 5), (64, 8)])
+@pytest.mark.parametrize("m,n,k", [(64, 3072, 3072), (200, 1024, 1280), (1, 48, 512),
+                                   (300, 400, 2048)])
+def test_split_k_bit_exact_two_calls(capi, cuda, tile_n, splits, m, n, k):
+    """Split-K partial sums are exact int32: identical accumulators to the unsplit GEMM.
+
+    Two calls on one workspace check that the per-tile counters return to zero.
+    """
+    a, b, sa, sb, bias = _operands(m, n, k, seed=m + n + splits, bias_dtype=torch.bfloat16)
+    need = ctypes.c_uint64()
+    assert capi.tm_scaled_mm_i8_splitk_workspace_size(m, n, k, tile_n, splits, ctypes.byref(need)) == 0
+    ws = torch.zeros(max(int(need.value), 16), dtype=torch.uint8, device=cuda)
+    d = [t.to(cuda) for t in (a, b, sa, sb, bias)]
+    acc_ref = orc.int_mm(a.numpy(), b.numpy())
+    ref = orc.scaled_mm_epilogue(acc_ref, sa.numpy(), sb.numpy(), bias, torch.bfloat16)
+    for _ in range(2):
+        out, acc = _splitk_call(capi, cuda, *d, tile_n, splits, ws)
+        np.testing.assert_array_equal(acc, acc_ref)
+        torch.testing.assert_close(out.float(), ref.float(), atol=ATOL, rtol=RTOL)
+    # too small a workspace for a forced split is an error, not a silent fallback
+    if need.value > 256:
+        small = torch.zeros(256, dtype=torch.uint8, device=cuda)
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=cuda)
+        rc = capi.tm_scaled_mm_i8_splitk(
+            out.data_ptr(), 0, d[0].data_ptr(), d[1].data_ptr(), d[2].data_ptr(), d[2].numel(),
+            d[3].data_ptr(), d[3].numel(), None, m, n, k, k, k, n, 0, None, tile_n, splits,
+            small.data_ptr(), small.numel(), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        assert rc == 8
+
+
+@pytest.mark.parametrize("m,n,k", [(64, 3072, 3072), (256, 12288, 3072), (16, 3072, 12288)])
+def test_skinny_m_heuristic_path(tm_ops, cuda, capi, m, n, k):
+    """The torch op picks split-K for skinny M on its own; results stay exact."""
+    need = ctypes.c_uint64()
+    assert capi.tm_scaled_mm_i8_workspace_size(m, n, k, ctypes.byref(need)) == 0
+    a, b, sa, sb, bias = _operands(m, n, k, seed=m * 3 + k, bias_dtype=torch.bfloat16)
+    for gelu in (False, True):
+        out, acc = _run(tm_ops, cuda, a, b, sa, sb, bias, torch.bfloat16, gelu=gelu)
+        acc_ref = orc.int_mm(a.numpy(), b.numpy())
+        np.testing.assert_array_equal(acc, acc_ref)
+        ref = orc.scaled_mm_epilogue(acc_ref, sa.numpy(), sb.numpy(), bias, torch.bfloat16, gelu=gelu)
+        torch.testing.assert_close(out.float(), ref.float(), atol=ATOL, rtol=RTOL)
