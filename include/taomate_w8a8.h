@@ -168,6 +168,32 @@ int tm_scaled_mm_i8_splitk_workspace_size(int64_t m, int64_t n, int64_t k, int t
                                           int splits, uint64_t* bytes);
 
 /*
+ * Split-K GEMM that allocates nothing, for callers that cannot call
+ * cudaMalloc: code running inside a host process whose device memory is
+ * owned and budgeted by someone else (an inference server's pre-partitioned
+ * pool, a plugin invoked from another runtime's launch path), or a latency-
+ * critical path where an allocation's implicit synchronisation is not
+ * acceptable.  Same computation and arguments as tm_scaled_mm_i8_splitk
+ * without the workspace and acc_debug: the int32 partials live in a
+ * TM_SPLITK_NOALLOC_MAX_BYTES (16 MiB) array compiled into the library,
+ * which every GPU that loads the library holds until the process exits.
+ * Requests whose split needs more than that (tile counters plus
+ * splits x m x n x 4 bytes) fail with TM_ERR_TOO_LARGE.  The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress), so make
+ * that first call before any stream capture.  Every call shares the one
+ * array and clears its counters on `stream` before use: calls that overlap
+ * on the GPU (other streams, other host threads) race and must be
+ * serialised by the caller.  No counterpart in the reference.
+ */
+#define TM_SPLITK_NOALLOC_MAX_BYTES (16ull << 20)
+int tm_scaled_mm_i8_splitk_noalloc(void* out, int out_dtype, const int8_t* a, const int8_t* b,
+                                   const float* scale_a, int64_t scale_a_numel,
+                                   const float* scale_b, int64_t scale_b_numel, const void* bias,
+                                   int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
+                                   int64_t ldo, uint32_t epilogue, int tile_n, int splits,
+                                   void* stream);
+
+/*
  * Row-parallel scaled GEMM with the reduce-scatter fused into the kernel
  * (the row-parallel fc2 / out-projection; the reference's
  * RowParallelLinear.forward = forward_local + tp all-reduce + bias,

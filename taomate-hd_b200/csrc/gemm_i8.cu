@@ -31,6 +31,7 @@
 #include <cuda_fp16.h>
 
 #include <cmath>
+#include <mutex>
 
 #include "common.h"
 #include "ptx.cuh"
@@ -1247,9 +1248,74 @@ int scaled_mm_impl(void* out, int out_dtype, const int8_t* a, const int8_t* b, c
 }
 
 }  // namespace
+
+// ---------------------------------------------------------------------------
+// Allocation-free split-K (tm_scaled_mm_i8_splitk_noalloc).
+//
+// Scratch for callers that must not allocate device memory: a fixed array in
+// the library's own device image, present on every GPU that loads the
+// library until the process exits.  Host code may not use the array's name as
+// a pointer (on the host it is only a stand-in for the symbol); its device
+// address is looked up once per device with cudaGetSymbolAddress while that
+// device is current.
+constexpr uint64_t kNoAllocScratchBytes = TM_SPLITK_NOALLOC_MAX_BYTES;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {};
+
+// Device address of this device's scratch array (resolved on first use).
+void* noalloc_scratch(int device) {
+  if (device < 0 || device >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[device] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess) return nullptr;
+    g_noalloc_ptr[device] = p;
+  }
+  return g_noalloc_ptr[device];
+}
+
+}  // namespace
 }  // namespace tmw
 
 extern "C" {
+
+int tm_scaled_mm_i8_splitk_noalloc(void* out, int out_dtype, const int8_t* a, const int8_t* b,
+                                   const float* scale_a, int64_t scale_a_numel,
+                                   const float* scale_b, int64_t scale_b_numel, const void* bias,
+                                   int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
+                                   int64_t ldo, uint32_t epilogue, int tile_n, int splits,
+                                   void* stream) {
+  if (tile_n != 256 && tile_n != 128 && tile_n != 64) return TM_ERR_UNSUPPORTED;
+  if (splits < 1 || splits > 64) return TM_ERR_UNSUPPORTED;
+  if (m < 0 || n <= 0 || k <= 0) return TM_ERR_SHAPE;
+  if (m > 0x7fffffffLL || n > 0x7fffffffLL || k > 0x7fffffffLL) return TM_ERR_TOO_LARGE;
+  if (m == 0) return TM_OK;
+  const int kblocks = static_cast<int>((k + tmw::kBK - 1) / tmw::kBK);
+  const tmw::SplitPlan plan =
+      tmw::plan_split(tile_n, splits, static_cast<int>(m), static_cast<int>(n), kblocks);
+  // m * n fits 64 bits; bound it before trusting splits * m * n * 4
+  const uint64_t mn = static_cast<uint64_t>(m) * static_cast<uint64_t>(n);
+  if (plan.splits > 1 &&
+      (mn > tmw::kNoAllocScratchBytes / 4 || plan.bytes > tmw::kNoAllocScratchBytes))
+    return TM_ERR_TOO_LARGE;
+  const int dev = tmw::current_device();
+  void* scratch = tmw::noalloc_scratch(dev);
+  if (scratch == nullptr) return TM_ERR_CUDA;
+  // The array keeps the previous call's contents: the per-tile counters must
+  // start at zero (the partial slices are fully rewritten by every call).
+  if (plan.splits > 1 &&
+      cudaMemsetAsync(scratch, 0, plan.counter_bytes, tmw::as_stream(stream)) != cudaSuccess)
+    return TM_ERR_CUDA;
+  const tmw::Workspace ws{scratch, tmw::kNoAllocScratchBytes, splits};
+  return tmw::scaled_mm_impl(out, out_dtype, a, b, scale_a, scale_a_numel, scale_b, scale_b_numel,
+                             bias, m, n, k, lda, ldb, ldo, epilogue, nullptr, tile_n,
+                             tmw::as_stream(stream), nullptr, &ws);
+}
+
 
 int tm_cutlass_scaled_mm(void* out, int out_dtype, const int8_t* a, const int8_t* b,
                          const float* scale_a, int64_t scale_a_numel, const float* scale_b,
