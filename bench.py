@@ -241,6 +241,57 @@ def run_reference(args) -> int:
 
 
 # ----------------------------------------------------------------- our arm
+SWEEP_M = (64, 256, 1024, 4096, 16384, 32768)
+SWEEP_NK = ((3072, 3072), (12288, 3072))  # (N, K)
+
+
+def skinny_sweep(world: int, device: torch.device, flush: torch.Tensor) -> list[dict]:
+    """the scaled GEMM over M at two weight shapes.
+
+    Each rank runs the column-parallel shard (N / TP) of its own weight; no
+    collective.  Every launch is timed alone with CUDA events.  Before each,
+    L2 is flushed by writing 256 MiB and then reading another 256 MiB, so the
+    weights come from HBM and no dirty flush lines are left for the timed
+    kernel to write back (at small M that write-back would dominate).
+    ``hbm_gbs`` counts the minimum bytes MK + NK + 2MN + 4M + 4N once per
+    launch.
+    """
+    from taomate_hd_b200 import ops
+
+    g = torch.Generator(device=device).manual_seed(77)
+    clean = torch.ones(FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+    sink = torch.empty((), dtype=torch.float32, device=device)
+    rows = []
+    reps = 10
+    for n_full, k in SWEEP_NK:
+        n = n_full // world
+        w = torch.randint(-127, 128, (n, k), generator=g, device=device, dtype=torch.int8)
+        sb = torch.rand(1, n, generator=g, device=device) * 1e-3 + 1e-5
+        for m in SWEEP_M:
+            a = torch.randint(-127, 128, (m, k), generator=g, device=device, dtype=torch.int8)
+            sa = torch.rand(m, 1, generator=g, device=device) * 1e-2 + 1e-4
+            for _ in range(3):
+                ops.scaled_mm(a, w.t(), sa, sb, torch.bfloat16)
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(reps)]
+            for e0, e1 in ev:
+                flush.zero_()
+                torch.sum(clean, out=sink)
+                e0.record()
+                ops.scaled_mm(a, w.t(), sa, sb, torch.bfloat16)
+                e1.record()
+            torch.cuda.synchronize()
+            us = 1e3 * max_over_ranks(sum(e0.elapsed_time(e1) for e0, e1 in ev) / reps,
+                                      world, device)
+            nbytes = m * k + n * k + 2 * m * n + 4 * m + 4 * n
+            rows.append({"m": m, "n": n, "k": k, "tp": world, "us": round(us, 2),
+                         "tops_per_gpu": round(2 * m * n * k / (us * 1e-6) / 1e12, 1),
+                         "hbm_gbs": round(nbytes / (us * 1e-6) / 1e9, 1)})
+            del a, sa
+        del w, sb
+    return rows
+
+
 def run_ours(args) -> int:
     world, rank, local = setup_distributed(args)
     if not torch.cuda.is_available():
@@ -299,28 +350,57 @@ def run_ours(args) -> int:
     total_ops = mlp.int8_ops
     value = total_ops / (step_ms * 1e-3) / 1e12
 
-    # e2e: same step through the public API, input from pinned host memory,
-    # output read back to pinned host memory, inside the timed region.
+    # e2e: the same step through the public API with this step's input copied in
+    # from pinned host memory and its output read back to pinned host memory,
+    # every step, inside the timed region.  The copies run on their own streams
+    # (host->device on one, device->host on another) into double-buffered device
+    # staging, so step i's read-back and step i+1's upload overlap the kernels as
+    # in a serving loop; the region spans all K steps and ends when the last
+    # read-back has landed.
     x_host = x.cpu().pin_memory()
-    x_dev = torch.empty_like(x)
     out_rows = mlp.out.shape[0] if world > 1 else TOKENS
-    y_host = torch.empty(out_rows, D, dtype=torch.bfloat16).pin_memory()
-    for _ in range(args.warmup):
-        x_dev.copy_(x_host, non_blocking=True)
-        y_host.copy_(mlp.forward(x_dev), non_blocking=True)
-    torch.cuda.synchronize()
-    barrier(world)
-    e_s = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
-    e_e = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
-    for i in range(K):
+    x_dev = [torch.empty_like(x) for _ in range(2)]
+    y_dev = [torch.empty(out_rows, D, dtype=torch.bfloat16, device=device) for _ in range(2)]
+    y_host = [torch.empty(out_rows, D, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    main = torch.cuda.current_stream(device)
+    up, down = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    x_ready = [torch.cuda.Event() for _ in range(2)]
+    x_free = [torch.cuda.Event() for _ in range(2)]
+    y_ready = [torch.cuda.Event() for _ in range(2)]
+    y_free = [torch.cuda.Event() for _ in range(2)]
+
+    def e2e_step(i: int) -> None:
+        b = i % 2
+        with torch.cuda.stream(up):
+            up.wait_event(x_free[b])
+            x_dev[b].copy_(x_host, non_blocking=True)
+            x_ready[b].record(up)
         flush.zero_()
-        e_s[i].record()
-        x_dev.copy_(x_host, non_blocking=True)
-        y_host.copy_(mlp.forward(x_dev), non_blocking=True)
-        e_e[i].record()
+        main.wait_event(x_ready[b])
+        y = mlp.forward(x_dev[b])
+        x_free[b].record(main)
+        main.wait_event(y_free[b])
+        y_dev[b].copy_(y)
+        y_ready[b].record(main)
+        with torch.cuda.stream(down):
+            down.wait_event(y_ready[b])
+            y_host[b].copy_(y_dev[b], non_blocking=True)
+            y_free[b].record(down)
+
+    for i in range(args.warmup):
+        e2e_step(i)
     torch.cuda.synchronize()
     barrier(world)
-    e2e_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(e_s, e_e)) / K, world, device)
+    e_start = torch.cuda.Event(enable_timing=True)
+    e_end = torch.cuda.Event(enable_timing=True)
+    e_start.record(main)
+    for i in range(K):
+        e2e_step(i)
+    main.wait_stream(down)
+    e_end.record(main)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(e_start.elapsed_time(e_end) / K, world, device)
 
     mlp_peer = mlp.peer
     extras = {}
@@ -344,11 +424,16 @@ def run_ours(args) -> int:
         torch.cuda.synchronize()
         barrier(world)
         block_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(bs, be)) / reps, world, device)
+        block_ops = block.int8_ops
+        del block
+        torch.cuda.empty_cache()
+        sweep = skinny_sweep(world, device, flush)
         extras = {"ms_per_768p_block_linear_chain": block_ms,
-                  "block_768p_tops": block.int8_ops / (block_ms * 1e-3) / 1e12,
+                  "block_768p_tops": block_ops / (block_ms * 1e-3) / 1e12,
                   "block_768p_config": f"M={BLOCK_TOKENS}, d={D}, QKV N={3 * HEADS * HEAD_DIM}, "
                                        f"out-proj, fc1 N={FFN} (+GELU), fc2; all-reduce after "
-                                       f"row-parallel linears; no LoRA / modulate fusion"}
+                                       f"row-parallel linears; no LoRA / modulate fusion",
+                  "skinny_sweep": sweep}
 
     if rank == 0:
         peaks = load_peaks()
@@ -388,7 +473,9 @@ def run_ours(args) -> int:
             "e2e": {"value": total_ops / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS",
                     "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": world * x.numel() * x.element_size(),
-                    "d2h_bytes_per_step": world * y_host.numel() * y_host.element_size()},
+                    "d2h_bytes_per_step": world * y_host[0].numel() * y_host[0].element_size(),
+                    "pipelining": "upload and read-back on their own streams, double-buffered; "
+                                  "L2 flushed inside the region before each step"},
             "gpu_launches": K * launches,
             "wall_s_timed_region": wall,
             "extras": extras,

@@ -225,6 +225,30 @@ int tm_scaled_mm_i8_reduce_scatter(void* out, const int8_t* a, const int8_t* b,
                                    int world, int rank, uint32_t epoch, int tile_n, void* stream);
 
 /*
+ * Row-parallel scaled GEMM with the all-reduce fused into the kernel (the
+ * reference's row-parallel out-projection: forward_local, then the tp
+ * all-reduce, then bias, src/taomate_hd/distributed/linear.py:279-289,
+ * collectives.py:19-40).  The reduce-scatter half is the one of
+ * tm_scaled_mm_i8_reduce_scatter; then each owner stores its reduced rows
+ * (bias added once) into every rank's output peer_out[j] ([m, n] bf16,
+ * row stride n) at their global row offset, drains once per CTA and adds
+ * the element count to peer_flags[j][world + rank].  The kernel returns
+ * when this rank's `world` gather counters show every owner's rows, so
+ * peer_out[rank] holds the full sum for the work that follows on `stream`.
+ * peer_flags[j]: rank j's 2 x world uint64 counters (reduce-scatter, then
+ *   gather), zeroed at allocation and never reset; peer_out[j]: rank j's
+ *   output buffer (local or IPC-mapped).  Same epoch / buffer-set /
+ *   alignment rules as tm_scaled_mm_i8_reduce_scatter; the output of a call
+ *   stays valid until the second call after it on the same buffer set pair.
+ */
+int tm_scaled_mm_i8_all_reduce(const int8_t* a, const int8_t* b, const float* scale_a,
+                               int64_t scale_a_numel, const float* scale_b, int64_t scale_b_numel,
+                               const void* bias, int64_t m, int64_t n, int64_t k, int64_t lda,
+                               int64_t ldb, void* const* peer_part, void* const* peer_flags,
+                               void* const* peer_out, int world, int rank, uint32_t epoch,
+                               int tile_n, void* stream);
+
+/*
  * Buffers shared between the ranks of a node for the fused reduction.
  * tm_peer_alloc: cudaMalloc `bytes`, zero them, and write the CUDA IPC
  * handle (tm_peer_handle_size() bytes) to handle_out.  tm_peer_open maps a

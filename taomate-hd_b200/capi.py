@@ -47,6 +47,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tm_scaled_mm_i8_ex": (c_int, [*_GEMM, c_u32, c_void_p, c_void_p]),
     "tm_scaled_mm_i8_tile": (c_int, [*_GEMM, c_u32, c_void_p, c_int, c_void_p]),
     "tm_quantize_weight_int8": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_i64, c_i64, c_void_p]),
+    "tm_scaled_mm_i8_all_reduce": (
+        c_int, [c_void_p, c_void_p, c_void_p, c_i64, c_void_p, c_i64, c_void_p,
+                c_i64, c_i64, c_i64, c_i64, c_i64, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                c_u32, c_int, c_void_p]),
     "tm_scaled_mm_i8_reduce_scatter": (
         c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_void_p, c_i64, c_void_p,
                 c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_void_p, c_void_p, c_int, c_int,

@@ -31,7 +31,9 @@
 #include <cuda_fp16.h>
 
 #include <cmath>
+#include <cstring>
 #include <mutex>
+#include <type_traits>
 
 #include "common.h"
 #include "ptx.cuh"
@@ -59,6 +61,10 @@ struct GemmArgs {
   int num_m, num_n, kblocks;  // tile grid (in units of the kernel's tile)
   uint32_t epilogue;
   int* status;
+  // Local output written by TMA stores of the staged blocks (the kernel's
+  // tm_out map) instead of per-lane stores; set only without split-K or
+  // scatter.
+  int tma_store;
   // Split-K (one-CTA kernel): each tile's K range is cut into `splits`
   // slices of kb_per_split k-blocks; every (tile, slice) unit stores its exact
   // int32 partial in ws[slice][M][N] and bumps tile_counters[tile]; the unit
@@ -84,6 +90,13 @@ struct GemmArgs {
   int64_t red_ldo;
   __nv_bfloat16* peer_part[kMaxPeers];
   unsigned long long* peer_count[kMaxPeers];
+  // Fused all-reduce (peer_out[0] != nullptr): every rank's full [M][N]
+  // output (ld N).  After reducing a block the owner stores it into all
+  // ranks' outputs at its global rows and, once its blocks are drained, adds
+  // the element count to peer_count[j][world + rank] (the gather counters);
+  // the kernel ends when this rank's gather counters show every owner's
+  // rows have arrived.
+  __nv_bfloat16* peer_out[kMaxPeers];
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
@@ -284,6 +297,160 @@ __device__ __forceinline__ uint4 ld_cg16(const void* p) {
   return r;
 }
 
+// ------------------------------------------------- TMA-store epilogue (local)
+// For local outputs each epilogue warp's 4 KiB shared region holds a 2 KiB
+// staging tile (32 rows x 64 bytes in the 64-byte swizzle layout a TMA
+// store reads) and a column cache: the per-column weight scales and bias of
+// the warp's kHalf columns.  The cache for tile t is filled from registers
+// that were loaded while tile t-1 was being processed, so the scale/bias
+// loads never sit between the accumulator and the math.
+constexpr int kStage64Bytes = 32 * 64;
+constexpr int kColCacheOffset = kStage64Bytes;            // kHalf <= 128 floats
+constexpr int kBiasCacheOffset = kColCacheOffset + 512;  // kHalf <= 128 x 16-bit
+static_assert(kBiasCacheOffset + 256 <= kEpiStageBytes, "epilogue warp region");
+
+__device__ __forceinline__ uint4* stage64_slot(uint8_t* stage, int row, int chunk) {
+  return reinterpret_cast<uint4*>(stage + row * 64 + ((chunk ^ ((row >> 1) & 3)) << 4));
+}
+
+// One lane's share of a tile's column constants: 4 scales, 4 bias values,
+// and the per-token scale of its row.
+struct ColPrefetch {
+  float4 sb;
+  uint2 bias;
+  float sa;
+};
+
+template <typename OutT>
+__device__ __forceinline__ ColPrefetch col_prefetch(const GemmArgs& g, int col_base, int cols,
+                                                    int64_t row, int lane) {
+  ColPrefetch p;
+  p.sb = make_float4(0.f, 0.f, 0.f, 0.f);
+  p.bias = make_uint2(0u, 0u);
+  const int c = col_base + 4 * lane;
+  if (4 * lane < cols && c < g.N) {  // N % 16 == 0: 4 columns are all in or all out
+    if (g.sb_per_col) {
+      p.sb = __ldg(reinterpret_cast<const float4*>(g.sb + c));
+    } else {
+      const float v = __ldg(g.sb);
+      p.sb = make_float4(v, v, v, v);
+    }
+    if (g.bias != nullptr) p.bias = __ldg(reinterpret_cast<const uint2*>(static_cast<const OutT*>(g.bias) + c));
+  }
+  p.sa = row < g.M ? (g.sa_per_row ? __ldg(g.sa + row) : __ldg(g.sa)) : 0.f;
+  return p;
+}
+
+__device__ __forceinline__ void col_cache_store(uint8_t* region, const ColPrefetch& p, int cols,
+                                                int lane) {
+  if (4 * lane < cols) {
+    *reinterpret_cast<float4*>(region + kColCacheOffset + 16 * lane) = p.sb;
+    *reinterpret_cast<uint2*>(region + kBiasCacheOffset + 8 * lane) = p.bias;
+  }
+}
+
+// Dequantise 16 columns with their constants from the column cache (all
+// lanes read the same words: shared-memory broadcasts).  Same arithmetic as
+// epilogue16.
+template <typename OutT>
+__device__ __forceinline__ void dequant16_cached(const GemmArgs& g, const uint32_t* r, float sa,
+                                                 const float* sb_s, const OutT* bias_s,
+                                                 uint4& o0, uint4& o1) {
+  float sb[16];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float4 v = reinterpret_cast<const float4*>(sb_s)[j];
+    sb[4 * j] = v.x;
+    sb[4 * j + 1] = v.y;
+    sb[4 * j + 2] = v.z;
+    sb[4 * j + 3] = v.w;
+  }
+  float y[16];
+  if (g.bias != nullptr) {
+    const uint4 b0 = reinterpret_cast<const uint4*>(bias_s)[0];
+    const uint4 b1 = reinterpret_cast<const uint4*>(bias_s)[1];
+    const OutT* be0 = reinterpret_cast<const OutT*>(&b0);
+    const OutT* be1 = reinterpret_cast<const OutT*>(&b1);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float b = out_to_f32<OutT>(j < 8 ? be0[j] : be1[j - 8]);
+      y[j] = __fmaf_rn(sa, __fmul_rn(sb[j], __int2float_rn(static_cast<int>(r[j]))), b);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      y[j] = __fmul_rn(sa, __fmul_rn(sb[j], __int2float_rn(static_cast<int>(r[j]))));
+  }
+  if (g.epilogue & TM_EPI_GELU_TANH) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) y[j] = gelu_tanh(round_out<OutT>(y[j]));
+  }
+  o0.x = pack2<OutT>(y[0], y[1]);
+  o0.y = pack2<OutT>(y[2], y[3]);
+  o0.z = pack2<OutT>(y[4], y[5]);
+  o0.w = pack2<OutT>(y[6], y[7]);
+  o1.x = pack2<OutT>(y[8], y[9]);
+  o1.y = pack2<OutT>(y[10], y[11]);
+  o1.z = pack2<OutT>(y[12], y[13]);
+  o1.w = pack2<OutT>(y[14], y[15]);
+}
+
+// One epilogue warp's share of a 128 x BN accumulator (lane quarter
+// warp % 4, column half (warp-2)/4), stored by TMA: per 32-column pass, one
+// TMEM load, dequantise from the column cache, stage, and one lane issues
+// a 32 x 32 bulk tensor store.  `release` (the accumulator-empty arrival)
+// runs as soon as the last TMEM load of the tile has landed, so the tensor
+// cores start the next tile while this one is converted and stored.  Rows
+// and columns past M/N are clipped by the TMA unit.  The column cache must
+// hold this tile's constants (col_cache_store) and `sa` this lane's row.
+template <int BN, typename OutT, typename Release>
+__device__ __forceinline__ void epilogue_tile_tma(const GemmArgs& g, const CUtensorMap* tm_out,
+                                                  uint32_t tmem_base, uint32_t acc_col,
+                                                  int64_t row0, int col0, int warp, int lane,
+                                                  uint8_t* region, float sa, Release release) {
+  constexpr int kHalf = BN / 2;
+  constexpr int kPasses = kHalf / 32;
+  static_assert(kHalf % 32 == 0 && kHalf <= 128, "32-column passes, cache of 128 columns");
+  const int q = warp & 3;
+  const int h = (warp - 2) >> 2;
+  const int64_t row_base = row0 + q * 32;
+  const int64_t row = row_base + lane;
+  int32_t* dbg_row = (g.acc_debug != nullptr && row < g.M)
+                         ? g.acc_debug + row * static_cast<int64_t>(g.N) : nullptr;
+  const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc_col +
+                         static_cast<uint32_t>(h * kHalf);
+  const float* sb_s = reinterpret_cast<const float*>(region + kColCacheOffset);
+  const OutT* bias_s = reinterpret_cast<const OutT*>(region + kBiasCacheOffset);
+#pragma unroll 1
+  for (int pass = 0; pass < kPasses; ++pass) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(pass * 32), r);
+    tmem_ld_wait();
+    if (pass == kPasses - 1) release();
+    const int col = col0 + h * kHalf + pass * 32;
+    uint4 o[4];
+    dequant16_cached<OutT>(g, r, sa, sb_s + pass * 32, bias_s + pass * 32, o[0], o[1]);
+    dequant16_cached<OutT>(g, r + 16, sa, sb_s + pass * 32 + 16, bias_s + pass * 32 + 16, o[2],
+                           o[3]);
+    if (dbg_row != nullptr) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4)
+        if (col + j < g.N)
+          *reinterpret_cast<uint4*>(dbg_row + col + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+    }
+    if (lane == 0) bulk_wait_read_all();  // the previous pass's store has left the tile
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 4; ++j) *stage64_slot(region, lane, j) = o[j];
+    fence_async_shared();
+    __syncwarp();
+    if (lane == 0 && row_base < g.M && col < g.N) {
+      tma_store_2d(tm_out, region, col, static_cast<int>(row_base));
+      bulk_commit();
+    }
+  }
+}
+
 // Fused reduce-scatter: after a CTA's epilogue warps have issued the stores
 // of all their blocks, one thread drains them (the named barrier orders
 // every warp's stores before that thread's system-scope fence; fences are
@@ -369,7 +536,23 @@ __device__ __forceinline__ void reduce_block(const GemmArgs& g, int lrb, int col
       __nv_bfloat162* op = reinterpret_cast<__nv_bfloat162*>(&o);
 #pragma unroll
       for (int j = 0; j < 4; ++j) op[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
-      *reinterpret_cast<uint4*>(g.red_out + (static_cast<int64_t>(lrb) * kBM + r) * g.red_ldo + c) = o;
+      if (g.peer_out[0] == nullptr) {
+        *reinterpret_cast<uint4*>(g.red_out + (static_cast<int64_t>(lrb) * kBM + r) * g.red_ldo +
+                                  c) = o;
+      } else {
+        // all-gather by push: this owner's rows into every rank's output,
+        // starting with the next rank so that the ranks' stores spread
+        // over the destinations
+        const int64_t go = (static_cast<int64_t>(g.rank) * g.rows_per_owner +
+                            static_cast<int64_t>(lrb) * kBM + r) * g.N + c;
+#pragma unroll
+        for (int d = 1; d <= W; ++d)
+          if (d <= g.world) {
+            int j = g.rank + d;
+            j = j >= g.world ? j - g.world : j;
+            *reinterpret_cast<uint4*>(g.peer_out[j] + go) = o;
+          }
+      }
     }
   }
 }
@@ -409,11 +592,13 @@ __device__ void reduce_phase(const GemmArgs& g, int bn, int cta, int ctas) {
     }
   }
   if (!__syncthreads_and(ok)) return;
+  unsigned long long reduced = 0;
   for (int t = cta; t < tiles; t += ctas) {
     const int lrb = t / g.num_n;
     const int nb = t - lrb * g.num_n;
     const int col0 = nb * bn;
     const int vec_per_row = min(bn, g.N - col0) / 8;
+    reduced += static_cast<unsigned long long>(kBM) * vec_per_row * 8;
     if (g.world <= 2)
       reduce_block<4, 2>(g, lrb, col0, vec_per_row);
     else if (g.world <= 4)
@@ -421,6 +606,31 @@ __device__ void reduce_phase(const GemmArgs& g, int bn, int cta, int ctas) {
     else
       reduce_block<1, 8>(g, lrb, col0, vec_per_row);
   }
+  if (g.peer_out[0] == nullptr) return;
+  // All-reduce: drain this CTA's gather stores once, publish the element
+  // count to every rank, then wait until every owner's rows are here.
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    for (int j = 0; j < g.world; ++j)
+      asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(g.peer_count[j] + g.world +
+                                                                     g.rank),
+                   "l"(reduced)
+                   : "memory");
+  }
+  if (threadIdx.x < static_cast<unsigned>(g.world)) {
+    const unsigned long long* c = g.peer_count[g.rank] + g.world + threadIdx.x;
+    bool seen = ld_acquire_sys_u64(c) >= target;
+    if (!seen) {
+      const uint64_t t0 = globaltimer_ns();
+      while (!(seen = ld_acquire_sys_u64(c) >= target)) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+        __nanosleep(64);
+      }
+    }
+    if (!seen && g.status) atomicExch(g.status, kDevWaitTimeout);
+  }
+  __syncthreads();
 }
 
 // Write a staged 32-row x (chunks x 16 bytes) block back as row segments:
@@ -540,7 +750,8 @@ struct Smem {
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kBarOffset = STAGES * kStageBytes;
   static constexpr int kBarBytes = (2 * STAGES + 4) * 8 + 16;
-  static constexpr int kEpiOffset = (kBarOffset + kBarBytes + 127) / 128 * 128;
+  // 1 KiB aligned: the staging tiles are read by TMA in the 128-byte swizzle
+  static constexpr int kEpiOffset = (kBarOffset + kBarBytes + 1023) / 1024 * 1024;
   static constexpr int kTotal = kEpiOffset + kEpiWarps * kEpiStageBytes + 1024;  // + align slack
   static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "swizzle atoms need 1 KiB alignment");
   static_assert(kTotal <= 227 * 1024, "shared memory budget");
@@ -578,7 +789,7 @@ __device__ __forceinline__ uint8_t* align1k(uint8_t* p) {
 template <int BN, int STAGES, typename OutT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                   const GemmArgs g) {
+                   const __grid_constant__ CUtensorMap tm_out, const GemmArgs g) {
   using L = Smem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1k(smem_raw);
@@ -605,6 +816,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_a);
     tma_prefetch_desc(&tm_b);
+    if (g.tma_store) tma_prefetch_desc(&tm_out);
   }
   if (warp == 1) {
     tmem_alloc(bar.tmem_slot, 2 * BN);
@@ -708,23 +920,58 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     long long sent[kMaxPeers] = {};
+    uint8_t* stage = smem + L::kEpiOffset + (warp - 2) * kEpiStageBytes;
+    // TMA-store epilogue: column constants of this warp's kHalf columns
+    // and its row's token scale, one tile ahead
+    constexpr int kHalf = BN / 2;
+    const int epi_h = (warp - 2) >> 2;
+    const int epi_row = (warp & 3) * 32 + lane;
+    ColPrefetch pf{};
+    if (g.tma_store && static_cast<int>(blockIdx.x) < units) {
+      int mb0, nb0;
+      tile_coords(static_cast<int>(blockIdx.x), g.num_m, g.num_n, mb0, nb0);
+      pf = col_prefetch<OutT>(g, nb0 * BN + epi_h * kHalf, kHalf,
+                              static_cast<int64_t>(mb0) * kBM + epi_row, lane);
+    }
     for (int unit = blockIdx.x; unit < units; unit += gridDim.x) {
       const int tile = unit / g.splits;
       int mb, nb;
       tile_coords(tile, g.num_m, g.num_n, mb, nb);
+      float sa_tile = 0.f;
+      if (g.tma_store) {
+        col_cache_store(stage, pf, kHalf, lane);
+        sa_tile = pf.sa;
+        __syncwarp();
+        const int next = unit + static_cast<int>(gridDim.x);
+        if (next < units) {
+          int mb1, nb1;
+          tile_coords(next, g.num_m, g.num_n, mb1, nb1);
+          pf = col_prefetch<OutT>(g, nb1 * BN + epi_h * kHalf, kHalf,
+                                  static_cast<int64_t>(mb1) * kBM + epi_row, lane);
+        }
+      }
       if (!mbar_wait(&bar.tmem_full[acc], acc_phase, bar.abort_flag, g.status)) break;
       tc_fence_after();
-      uint8_t* stage = smem + L::kEpiOffset + (warp - 2) * kEpiStageBytes;
       if (g.splits > 1)
         splitk_epilogue<BN, OutT>(g, tmem_base, static_cast<uint32_t>(acc * BN),
                                   static_cast<int64_t>(mb) * kBM, nb * BN, tile,
                                   unit - tile * g.splits, warp, lane, stage, bar.split_last);
-      else
+      const auto release = [&]() {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar.tmem_empty[acc]);
+      };
+      if (g.splits > 1) {
+        release();
+      } else if (g.tma_store) {
+        epilogue_tile_tma<BN, OutT>(g, &tm_out, tmem_base, static_cast<uint32_t>(acc * BN),
+                                    static_cast<int64_t>(mb) * kBM, nb * BN, warp, lane, stage,
+                                    sa_tile, release);
+      } else {
         epilogue_tile<BN, OutT>(g, tmem_base, static_cast<uint32_t>(acc * BN),
                                 static_cast<int64_t>(mb) * kBM, nb * BN, warp, lane, stage);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar.tmem_empty[acc]);
+        release();
+      }
       if (g.world > 0 && static_cast<int64_t>(mb) * kBM < g.M)
         sent[static_cast<int>(static_cast<int64_t>(mb) * kBM / g.rows_per_owner)] +=
             kBM * min(BN, g.N - nb * BN);
@@ -733,6 +980,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         acc_phase ^= 1u;
       }
     }
+    if (g.tma_store && lane == 0) bulk_wait_all();  // stores done before the CTA ends
     if (g.world > 0) publish_counts(g, sent, warp, lane);
   }
 
@@ -755,7 +1003,8 @@ struct PairTmem {
 template <int BN, int STAGES, typename OutT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tm_a,
-                        const __grid_constant__ CUtensorMap tm_b, const GemmArgs g) {
+                        const __grid_constant__ CUtensorMap tm_b,
+                        const __grid_constant__ CUtensorMap tm_out, const GemmArgs g) {
   constexpr int kBNHalf = BN / 2;
   using L = Smem<kBNHalf, STAGES>;
   extern __shared__ uint8_t smem_raw[];
@@ -787,6 +1036,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_a);
     tma_prefetch_desc(&tm_b);
+    if (g.tma_store) tma_prefetch_desc(&tm_out);
   }
   if (warp == 1) {
     tmem_alloc_pair(bar.tmem_slot, PairTmem<BN>::kCols);
@@ -895,17 +1145,50 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     long long sent[kMaxPeers] = {};
+    uint8_t* stage = smem + L::kEpiOffset + (warp - 2) * kEpiStageBytes;
+    // TMA-store epilogue: column constants of this warp's kHalf columns
+    // and its row's token scale, one tile ahead
+    constexpr int kHalf = BN / 2;
+    const int epi_h = (warp - 2) >> 2;
+    const int epi_row = static_cast<int>(rank) * kBM + (warp & 3) * 32 + lane;
+    ColPrefetch pf{};
+    if (g.tma_store && pair < tiles) {
+      int mb0, nb0;
+      tile_coords(pair, g.num_m, g.num_n, mb0, nb0);
+      pf = col_prefetch<OutT>(g, nb0 * BN + epi_h * kHalf, kHalf,
+                              static_cast<int64_t>(mb0) * 2 * kBM + epi_row, lane);
+    }
     for (int tile = pair; tile < tiles; tile += pairs) {
       int mb, nb;
       tile_coords(tile, g.num_m, g.num_n, mb, nb);
+      float sa_tile = 0.f;
+      if (g.tma_store) {
+        col_cache_store(stage, pf, kHalf, lane);
+        sa_tile = pf.sa;
+        __syncwarp();
+        if (tile + pairs < tiles) {
+          int mb1, nb1;
+          tile_coords(tile + pairs, g.num_m, g.num_n, mb1, nb1);
+          pf = col_prefetch<OutT>(g, nb1 * BN + epi_h * kHalf, kHalf,
+                                  static_cast<int64_t>(mb1) * 2 * kBM + epi_row, lane);
+        }
+      }
       if (!mbar_wait(&bar.tmem_full[acc], acc_phase, bar.abort_flag, g.status)) break;
       tc_fence_after();
       const int64_t row0 = static_cast<int64_t>(mb) * 2 * kBM + rank * kBM;
-      epilogue_tile<BN, OutT>(g, tmem_base, static_cast<uint32_t>(acc * BN), row0, nb * BN, warp,
-                              lane, smem + L::kEpiOffset + (warp - 2) * kEpiStageBytes);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(acc == 0 ? empty_leader0 : empty_leader1);
+      const auto release = [&]() {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(acc == 0 ? empty_leader0 : empty_leader1);
+      };
+      if (g.tma_store) {
+        epilogue_tile_tma<BN, OutT>(g, &tm_out, tmem_base, static_cast<uint32_t>(acc * BN), row0,
+                                    nb * BN, warp, lane, stage, sa_tile, release);
+      } else {
+        epilogue_tile<BN, OutT>(g, tmem_base, static_cast<uint32_t>(acc * BN), row0, nb * BN, warp,
+                                lane, stage);
+        release();
+      }
       if (g.world > 0 && row0 < g.M)
         sent[static_cast<int>(row0 / g.rows_per_owner)] += kBM * min(BN, g.N - nb * BN);
       if (++acc == 2) {
@@ -913,6 +1196,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         acc_phase ^= 1u;
       }
     }
+    if (g.tma_store && lane == 0) bulk_wait_all();  // stores done before the CTA ends
     if (g.world > 0) publish_counts(g, sent, warp, lane);
   }
 
@@ -933,6 +1217,21 @@ struct Operands {
   int64_t ldb;
 };
 
+// Output map for the TMA-store epilogue (32 x 32 boxes, 64-byte swizzle),
+// or switch that epilogue off where it does not apply: split-K and scatter
+// outputs.  The map is left zeroed (and never read) when unused.
+template <int BN, typename OutT>
+bool encode_out_map(CUtensorMap* map, GemmArgs& args) {
+  memset(map, 0, sizeof(*map));
+  args.tma_store = args.world == 0 && args.splits == 1;
+  if (!args.tma_store) return true;
+  const CUtensorMapDataType dt = std::is_same<OutT, __nv_bfloat16>::value
+                                     ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return encode_tmap_2d(map, dt, args.out, args.N, args.M, static_cast<uint64_t>(args.ldo) * 2, 32,
+                        32, CU_TENSOR_MAP_SWIZZLE_64B);
+}
+
 template <int BN, int STAGES, typename OutT>
 int launch_single(const Operands& op, GemmArgs args, int sms, cudaStream_t stream) {
   using L = Smem<BN, STAGES>;
@@ -944,6 +1243,8 @@ int launch_single(const Operands& op, GemmArgs args, int sms, cudaStream_t strea
       !encode_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, op.b, args.K, args.N, op.ldb, kBK, BN,
                       CU_TENSOR_MAP_SWIZZLE_128B))
     return TM_ERR_CUDA;
+  CUtensorMap to;
+  if (!encode_out_map<BN, OutT>(&to, args)) return TM_ERR_CUDA;
   auto kernel = gemm_i8_kernel<BN, STAGES, OutT>;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal) !=
       cudaSuccess)
@@ -961,7 +1262,7 @@ int launch_single(const Operands& op, GemmArgs args, int sms, cudaStream_t strea
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = args.world > 0 ? 1 : 0;
-  if (cudaLaunchKernelEx(&cfg, kernel, ta, tb, args) != cudaSuccess) return TM_ERR_CUDA;
+  if (cudaLaunchKernelEx(&cfg, kernel, ta, tb, to, args) != cudaSuccess) return TM_ERR_CUDA;
   return check_launch();
 }
 
@@ -976,6 +1277,8 @@ int launch_pair(const Operands& op, GemmArgs args, int max_pairs, cudaStream_t s
       !encode_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, op.b, args.K, args.N, op.ldb, kBK,
                       BN / 2, CU_TENSOR_MAP_SWIZZLE_128B))
     return TM_ERR_CUDA;
+  CUtensorMap to;
+  if (!encode_out_map<BN, OutT>(&to, args)) return TM_ERR_CUDA;
   auto kernel = gemm_i8_pair_kernel<BN, STAGES, OutT>;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal) !=
       cudaSuccess)
@@ -998,7 +1301,7 @@ int launch_pair(const Operands& op, GemmArgs args, int max_pairs, cudaStream_t s
   attr[1].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = args.world > 0 ? 2 : 1;
-  if (cudaLaunchKernelEx(&cfg, kernel, ta, tb, args) != cudaSuccess) return TM_ERR_CUDA;
+  if (cudaLaunchKernelEx(&cfg, kernel, ta, tb, to, args) != cudaSuccess) return TM_ERR_CUDA;
   return check_launch();
 }
 
@@ -1144,6 +1447,7 @@ struct ScatterSpec {
   int world;
   int rank;
   uint32_t epoch;
+  void* const* peer_out = nullptr;  // all-reduce: every rank's [M][N] output
 };
 
 // Optional split-K workspace (zeroed by the caller before its first use; the
@@ -1178,6 +1482,10 @@ int scaled_mm_impl(void* out, int out_dtype, const int8_t* a, const int8_t* b, c
       if (!scatter->peer_part[j] || !scatter->peer_flags[j]) return TM_ERR_NULL_POINTER;
       if (!aligned16(scatter->peer_part[j]) || !aligned16(scatter->peer_flags[j]))
         return TM_ERR_ALIGNMENT;
+      if (scatter->peer_out != nullptr) {
+        if (!scatter->peer_out[j]) return TM_ERR_NULL_POINTER;
+        if (!aligned16(scatter->peer_out[j])) return TM_ERR_ALIGNMENT;
+      }
     }
   }
   if (m == 0) return TM_OK;
@@ -1215,6 +1523,8 @@ int scaled_mm_impl(void* out, int out_dtype, const int8_t* a, const int8_t* b, c
     for (int j = 0; j < scatter->world; ++j) {
       args.peer_part[j] = static_cast<__nv_bfloat16*>(scatter->peer_part[j]);
       args.peer_count[j] = static_cast<unsigned long long*>(scatter->peer_flags[j]);
+      if (scatter->peer_out != nullptr)
+        args.peer_out[j] = static_cast<__nv_bfloat16*>(scatter->peer_out[j]);
     }
   }
   const int max_pairs = max_resident_pairs(dev, sms);
@@ -1344,6 +1654,24 @@ int tm_scaled_mm_i8_reduce_scatter(void* out, const int8_t* a, const int8_t* b,
   const tmw::ScatterSpec spec{peer_part, peer_flags, world, rank, epoch};
   return tmw::scaled_mm_impl(out, TM_DTYPE_BF16, a, b, scale_a, scale_a_numel, scale_b,
                              scale_b_numel, bias, m, n, k, lda, ldb, ldo, 0u, nullptr, tile_n,
+                             tmw::as_stream(stream), &spec);
+}
+
+int tm_scaled_mm_i8_all_reduce(const int8_t* a, const int8_t* b, const float* scale_a,
+                               int64_t scale_a_numel, const float* scale_b, int64_t scale_b_numel,
+                               const void* bias, int64_t m, int64_t n, int64_t k, int64_t lda,
+                               int64_t ldb, void* const* peer_part, void* const* peer_flags,
+                               void* const* peer_out, int world, int rank, uint32_t epoch,
+                               int tile_n, void* stream) {
+  if (peer_out == nullptr) return TM_ERR_NULL_POINTER;
+  if (world < 1 || world > tmw::kMaxPeers) return TM_ERR_TOO_LARGE;
+  if (rank < 0 || rank >= world) return TM_ERR_SHAPE;
+  if (peer_out[rank] == nullptr) return TM_ERR_NULL_POINTER;
+  const tmw::ScatterSpec spec{peer_part, peer_flags, world, rank, epoch, peer_out};
+  // the owner's reduced rows land in its own output at their global offset
+  void* own_rows = static_cast<__nv_bfloat16*>(peer_out[rank]) + rank * (m / world) * n;
+  return tmw::scaled_mm_impl(own_rows, TM_DTYPE_BF16, a, b, scale_a, scale_a_numel, scale_b,
+                             scale_b_numel, bias, m, n, k, lda, ldb, n, 0u, nullptr, tile_n,
                              tmw::as_stream(stream), &spec);
 }
 

@@ -14,7 +14,8 @@ the same linears inside its DiT block, model/layers.py:346-368, :502-523):
                        in its GEMM epilogue so that it enters the sum once.
 * ``TPW8A8AttnProj``   merged QKV column-parallel (each of Q, K, V sharded
                        separately, linear.py:207-215) and the row-parallel
-                       out-projection with an all-reduce.
+                       out-projection with an all-reduce (NCCL, or fused into
+                       the GEMM launch over NVLink peer memory).
 * ``TPW8A8BlockChain`` QKV, out-proj, fc1, fc2 of one block in sequence.
 
 Every ``forward`` writes into buffers allocated at construction, so a step
@@ -108,6 +109,9 @@ def _gemm(q: _Quant, w: W8Weight, out: torch.Tensor, *, bias: torch.Tensor | Non
     return out
 
 
+_MLP_REDUCE = ("reduce_scatter", "fused_reduce_scatter", "all_reduce", "fused_all_reduce")
+
+
 class TPW8A8MLP:
     """480p LOW-stage MLP, fc1 column + fc2 row (reduce-scatter)."""
 
@@ -116,8 +120,8 @@ class TPW8A8MLP:
         t = ctx.tp_world_size
         if ffn % t or (reduce == "reduce_scatter" and tokens % t):
             raise ValueError("ffn and tokens must divide by the TP degree")
-        if reduce not in ("reduce_scatter", "all_reduce", "fused_reduce_scatter"):
-            raise ValueError("reduce must be 'reduce_scatter', 'fused_reduce_scatter' or 'all_reduce'")
+        if reduce not in _MLP_REDUCE:
+            raise ValueError(f"reduce must be one of {_MLP_REDUCE}")
         self.ctx, self.tokens, self.d, self.ffn, self.reduce = ctx, tokens, d, ffn, reduce
         self.fc1 = column_weight(ffn, d, ctx, seed + 10, device, bias=True)
         self.fc2 = row_weight(d, ffn, ctx, seed + 20, device, bias=True)
@@ -134,6 +138,11 @@ class TPW8A8MLP:
             from .peer_reduce import PeerReduceScatter
 
             self.peer = PeerReduceScatter(ctx, tokens, d, device)
+        self.peer_ar = None
+        if reduce == "fused_all_reduce" and t > 1:
+            from .peer_reduce import PeerAllReduce
+
+            self.peer_ar = PeerAllReduce(ctx, tokens, d, device)
 
     @property
     def int8_ops(self) -> int:
@@ -160,6 +169,11 @@ class TPW8A8MLP:
             if gemm_events is not None:
                 gemm_events[3].record()
             return self.out
+        if self.peer_ar is not None:
+            y = self.peer_ar(self.q2.q, self.q2.s, self.fc2.q, self.fc2.scale, self.fc2.bias)
+            if gemm_events is not None:
+                gemm_events[3].record()
+            return y
         bias2 = self.fc2.bias if self.ctx.tp_rank == 0 else None
         _gemm(self.q2, self.fc2, self.partial, bias=bias2)
         if gemm_events is not None:
@@ -177,11 +191,13 @@ class TPW8A8AttnProj:
     """merged QKV column-parallel + out-proj row-parallel (all-reduce)."""
 
     def __init__(self, tokens: int, d: int, heads: int, head_dim: int, ctx: ParallelContext,
-                 device: torch.device, *, seed: int = 0):
+                 device: torch.device, *, seed: int = 0, reduce: str = "all_reduce"):
         t = ctx.tp_world_size
         width = heads * head_dim
         if heads % t:
             raise ValueError("heads must divide by the TP degree")
+        if reduce not in ("all_reduce", "fused_all_reduce"):
+            raise ValueError("reduce must be 'all_reduce' or 'fused_all_reduce'")
         self.ctx, self.tokens, self.d, self.width = ctx, tokens, d, width
         self.qkv = column_weight(3 * width, d, ctx, seed + 30, device, bias=True,
                                  output_sizes=(width, width, width))
@@ -190,6 +206,11 @@ class TPW8A8AttnProj:
         self.qkv_out = torch.empty(tokens, 3 * width // t, dtype=torch.bfloat16, device=device)
         self.q_attn = _Quant(tokens, width // t, device)
         self.partial = torch.empty(tokens, d, dtype=torch.bfloat16, device=device)
+        self.peer_ar = None
+        if reduce == "fused_all_reduce" and t > 1:
+            from .peer_reduce import PeerAllReduce
+
+            self.peer_ar = PeerAllReduce(ctx, tokens, d, device)
 
     @property
     def int8_ops(self) -> int:
@@ -203,6 +224,10 @@ class TPW8A8AttnProj:
         _gemm(self.q_in, self.qkv, self.qkv_out, bias=self.qkv.bias)
         a = self.qkv_out[:, : self.width // self.ctx.tp_world_size] if attn is None else attn
         self.q_attn(a)
+        if self.peer_ar is not None:
+            # partial blocks go to their row owners, reduced rows to every rank
+            return self.peer_ar(self.q_attn.q, self.q_attn.s, self.out_proj.q,
+                                self.out_proj.scale, self.out_proj.bias)
         bias = self.out_proj.bias if self.ctx.tp_rank == 0 else None
         _gemm(self.q_attn, self.out_proj, self.partial, bias=bias)
         t = self.ctx.tp_world_size
@@ -215,9 +240,12 @@ class TPW8A8BlockChain:
     """BASELINE configs[3] linear chain of one DiT block: QKV, out-proj, fc1, fc2."""
 
     def __init__(self, tokens: int, d: int, heads: int, head_dim: int, ffn: int,
-                 ctx: ParallelContext, device: torch.device, *, seed: int = 0):
-        self.attn = TPW8A8AttnProj(tokens, d, heads, head_dim, ctx, device, seed=seed)
-        self.mlp = TPW8A8MLP(tokens, d, ffn, ctx, device, seed=seed + 100, reduce="all_reduce")
+                 ctx: ParallelContext, device: torch.device, *, seed: int = 0,
+                 fused: bool = False):
+        reduce = "fused_all_reduce" if fused else "all_reduce"
+        self.attn = TPW8A8AttnProj(tokens, d, heads, head_dim, ctx, device, seed=seed,
+                                   reduce=reduce)
+        self.mlp = TPW8A8MLP(tokens, d, ffn, ctx, device, seed=seed + 100, reduce=reduce)
 
     @property
     def int8_ops(self) -> int:

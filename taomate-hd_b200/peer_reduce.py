@@ -1,21 +1,25 @@
-"""Fused row-parallel reduce-scatter over NVLink peer memory.
+"""Fused row-parallel reduce-scatter / all-reduce over NVLink peer memory.
 
 The row-parallel linears of the reference sum their partial outputs with an
 NCCL all-reduce after the GEMM (src/taomate_hd/distributed/linear.py:279-289,
-collectives.py:19-40).  ``PeerReduceScatter`` runs the reduction inside the
-scaled-GEMM kernel instead (``tm_scaled_mm_i8_reduce_scatter`` in
-``include/taomate_w8a8.h``): the epilogue pushes each bf16 partial block to
-the rank that owns those rows over NVLink while the GEMM keeps running;
-each CTA then drains its stores once and bumps per-source counters on the
-owners; CTAs out of GEMM tiles wait for the counters and reduce their own
-rows from local memory.
+collectives.py:19-40).  These classes run the reduction inside the
+scaled-GEMM kernel instead:
+
+* ``PeerReduceScatter`` (``tm_scaled_mm_i8_reduce_scatter``): the epilogue
+  pushes each bf16 partial block to the rank that owns those rows over
+  NVLink while the GEMM keeps running; each CTA then drains its stores once
+  and bumps per-source counters on the owners; CTAs out of GEMM tiles wait
+  for the counters and reduce their own rows from local memory.
+* ``PeerAllReduce`` (``tm_scaled_mm_i8_all_reduce``): the same, after which
+  every owner pushes its reduced rows into every rank's full output and the
+  kernel returns once all owners' rows have arrived.
 
 Each rank allocates one buffer holding two sets (alternate calls) of
-``world`` receive slots (``rows x cols`` bf16 in total) plus ``world``
-64-bit counters, shares it by CUDA IPC handle over the TP process group,
-and maps every peer's buffer once.  All ranks must call in the same order
-with the same shapes and tile configuration; the per-set use counts are
-kept identically on every rank.
+``world`` receive slots (``rows x cols`` bf16 in total), the counters and,
+for the all-reduce, a ``rows x cols`` output; shares it by CUDA IPC handle
+over the TP process group, and maps every peer's buffer once.  All ranks must
+call in the same order with the same shapes and tile configuration; the
+per-set use counts are kept identically on every rank.
 """
 from __future__ import annotations
 
@@ -31,13 +35,30 @@ def _align(value: int, to: int = 256) -> int:
     return (value + to - 1) // to * to
 
 
-class PeerReduceScatter:
-    """Symmetric receive buffers + the fused GEMM/reduce-scatter for one shape."""
+class _DeviceArray:
+    """``__cuda_array_interface__`` over memory this module allocated."""
+
+    def __init__(self, ptr: int, shape: tuple[int, ...]):
+        self.__cuda_array_interface__ = {
+            "shape": shape, "typestr": "<i2", "data": (ptr, False), "version": 3, "strides": None}
+
+
+def _wrap_bf16(ptr: int, rows: int, cols: int, device: torch.device) -> torch.Tensor:
+    """A bf16 ``[rows, cols]`` tensor aliasing device memory at ``ptr`` (no copy)."""
+    with torch.cuda.device(device):
+        t = torch.as_tensor(_DeviceArray(ptr, (rows, cols)), device=device)
+    return t.view(torch.bfloat16)
+
+
+class _PeerBuffers:
+    """Two buffer sets per rank, shared across the TP group by CUDA IPC."""
+
+    _gather = False
 
     def __init__(self, ctx: ParallelContext, rows: int, cols: int, device: torch.device):
         world, rank = ctx.tp_world_size, ctx.tp_rank
         if world < 1 or world > 8:
-            raise ValueError("the fused reduce-scatter supports 1..8 ranks")
+            raise ValueError("the fused reduction supports 1..8 ranks")
         if rows % (256 * world):
             raise ValueError(f"rows ({rows}) must be a multiple of 256 * world ({256 * world})")
         if cols % 16:
@@ -46,9 +67,11 @@ class PeerReduceScatter:
         self.world, self.rank = world, rank
         self.rows_per_owner = rows // world
         self._lib = _native.capi()
+        self._own = None
         part_bytes = _align(rows * cols * 2)
-        count_bytes = _align(world * 8)
-        self._half = part_bytes + count_bytes
+        count_bytes = _align(world * 8 * (2 if self._gather else 1))
+        out_bytes = part_bytes if self._gather else 0
+        self._half = part_bytes + count_bytes + out_bytes
         handle_size = self._lib.tm_peer_handle_size()
         handle = (ctypes.c_char * handle_size)()
         base = ctypes.c_void_p()
@@ -81,37 +104,25 @@ class PeerReduceScatter:
         arr = ctypes.c_void_p * world
         self._part = [arr(*[b + h * self._half for b in bases]) for h in (0, 1)]
         self._counts = [arr(*[b + h * self._half + part_bytes for b in bases]) for h in (0, 1)]
+        self._outs = [arr(*[b + h * self._half + part_bytes + count_bytes for b in bases])
+                      for h in (0, 1)] if self._gather else None
         self.calls = 0
         self._uses = [0, 0]
 
-    def __call__(self, q: torch.Tensor, q_scale: torch.Tensor, w_q: torch.Tensor,
-                 w_scale: torch.Tensor, bias: torch.Tensor | None, out: torch.Tensor,
-                 tile_n: int = 0) -> torch.Tensor:
-        """``out[rows/world, cols] = (sum over ranks of this row block of q @ w_q^T) + bias``.
-
-        ``q``: int8 ``[rows, k]`` local activations; ``q_scale``: fp32 per-token
-        (or one) scales; ``w_q``: int8 ``[cols, k]`` local weight shard;
-        ``w_scale``: fp32 ``[cols]``; ``bias``: bf16 ``[cols]`` or None.
-        """
+    def _check(self, q: torch.Tensor, w_q: torch.Tensor) -> tuple[int, int]:
         m, k = q.shape
         if m != self.rows or w_q.shape[0] != self.cols or w_q.shape[1] != k:
             raise ValueError("shape differs from the one the buffers were built for")
-        if out.shape != (self.rows_per_owner, self.cols) or out.dtype != torch.bfloat16:
-            raise ValueError(f"out must be bf16 [{self.rows_per_owner}, {self.cols}]")
+        return m, k
+
+    def _next_set(self) -> tuple[int, ctypes.c_void_p]:
         self.calls += 1
         half = self.calls & 1
         self._uses[half] += 1
-        stream = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
-        rc = self._lib.tm_scaled_mm_i8_reduce_scatter(
-            out.data_ptr(), q.data_ptr(), w_q.data_ptr(), q_scale.data_ptr(), q_scale.numel(),
-            w_scale.data_ptr(), w_scale.numel(), None if bias is None else bias.data_ptr(),
-            m, self.cols, k, q.stride(0), w_q.stride(0), out.stride(0),
-            self._part[half], self._counts[half], self.world, self.rank, self._uses[half],
-            tile_n, stream)
-        if rc != 0:
-            raise RuntimeError(
-                f"tm_scaled_mm_i8_reduce_scatter failed: {self._lib.tm_status_string(rc).decode()}")
-        return out
+        return half, ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+
+    def _raise(self, name: str, rc: int) -> None:
+        raise RuntimeError(f"{name} failed: {self._lib.tm_status_string(rc).decode()}")
 
     def close(self) -> None:
         """Unmap the peers' buffers and free this rank's (after a device sync)."""
@@ -129,3 +140,62 @@ class PeerReduceScatter:
             self.close()
         except Exception:
             pass
+
+
+class PeerReduceScatter(_PeerBuffers):
+    """Symmetric receive buffers + the fused GEMM/reduce-scatter for one shape."""
+
+    def __call__(self, q: torch.Tensor, q_scale: torch.Tensor, w_q: torch.Tensor,
+                 w_scale: torch.Tensor, bias: torch.Tensor | None, out: torch.Tensor,
+                 tile_n: int = 0) -> torch.Tensor:
+        """``out[rows/world, cols] = (sum over ranks of this row block of q @ w_q^T) + bias``.
+
+        ``q``: int8 ``[rows, k]`` local activations; ``q_scale``: fp32 per-token
+        (or one) scales; ``w_q``: int8 ``[cols, k]`` local weight shard;
+        ``w_scale``: fp32 ``[cols]``; ``bias``: bf16 ``[cols]`` or None.
+        """
+        m, k = self._check(q, w_q)
+        if out.shape != (self.rows_per_owner, self.cols) or out.dtype != torch.bfloat16:
+            raise ValueError(f"out must be bf16 [{self.rows_per_owner}, {self.cols}]")
+        half, stream = self._next_set()
+        rc = self._lib.tm_scaled_mm_i8_reduce_scatter(
+            out.data_ptr(), q.data_ptr(), w_q.data_ptr(), q_scale.data_ptr(), q_scale.numel(),
+            w_scale.data_ptr(), w_scale.numel(), None if bias is None else bias.data_ptr(),
+            m, self.cols, k, q.stride(0), w_q.stride(0), out.stride(0),
+            self._part[half], self._counts[half], self.world, self.rank, self._uses[half],
+            tile_n, stream)
+        if rc != 0:
+            self._raise("tm_scaled_mm_i8_reduce_scatter", rc)
+        return out
+
+
+class PeerAllReduce(_PeerBuffers):
+    """Symmetric buffers + the fused GEMM/all-reduce for one shape.
+
+    The result lives in this object's output buffers (two, alternating by
+    call): a call's output stays valid until the second call after it.
+    """
+
+    _gather = True
+
+    def __init__(self, ctx: ParallelContext, rows: int, cols: int, device: torch.device):
+        super().__init__(ctx, rows, cols, device)
+        # tensor views over this rank's own output of each set (the memory
+        # belongs to this object and is freed by close())
+        self._views = [_wrap_bf16(self._outs[h][self.rank], self.rows, self.cols, device)
+                       for h in (0, 1)]
+
+    def __call__(self, q: torch.Tensor, q_scale: torch.Tensor, w_q: torch.Tensor,
+                 w_scale: torch.Tensor, bias: torch.Tensor | None,
+                 tile_n: int = 0) -> torch.Tensor:
+        """``[rows, cols] = (sum over ranks of q @ w_q^T) + bias`` on every rank."""
+        m, k = self._check(q, w_q)
+        half, stream = self._next_set()
+        rc = self._lib.tm_scaled_mm_i8_all_reduce(
+            q.data_ptr(), w_q.data_ptr(), q_scale.data_ptr(), q_scale.numel(),
+            w_scale.data_ptr(), w_scale.numel(), None if bias is None else bias.data_ptr(),
+            m, self.cols, k, q.stride(0), w_q.stride(0), self._part[half], self._counts[half],
+            self._outs[half], self.world, self.rank, self._uses[half], tile_n, stream)
+        if rc != 0:
+            self._raise("tm_scaled_mm_i8_all_reduce", rc)
+        return self._views[half]

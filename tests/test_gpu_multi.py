@@ -1,11 +1,14 @@
-"""GPU, 2 ranks on 2 GPUs: the fused row-parallel reduce-scatter.
+"""GPU, 2 ranks on 2 GPUs: the fused row-parallel reduce-scatter and all-reduce.
 
 Each rank holds a K-shard of a row-parallel W8A8 linear (linear.py:259-289
 semantics: per-token activation scales and per-channel weight scales over the
 local K slice).  ``PeerReduceScatter`` must produce, on every rank, the sum
 over ranks of the bf16 partials for its row block plus the bias: checked
 against the CPU oracle and against the NCCL reduce-scatter path, over several
-consecutive calls (alternating buffer sets, advancing epochs).  Runs as child
+consecutive calls (alternating buffer sets, advancing epochs).  ``PeerAllReduce``
+must leave the full sum (plus bias) on every rank, checked the same way against
+the oracle and NCCL's all-reduce; the output of a call must survive the next
+call (alternating output sets).  Runs as child
 processes with NCCL's NVLS disabled; skipped with fewer than 2 GPUs.
 """
 from __future__ import annotations
@@ -45,9 +48,9 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
             device_id=device)
         from oracle import w8a8_oracle as orc
         from taomate_hd_b200 import _native, ops
-        from taomate_hd_b200.collectives import reduce_scatter_rows
+        from taomate_hd_b200.collectives import all_reduce_sum, reduce_scatter_rows
         from taomate_hd_b200.parallel import ParallelContext
-        from taomate_hd_b200.peer_reduce import PeerReduceScatter
+        from taomate_hd_b200.peer_reduce import PeerAllReduce, PeerReduceScatter
 
         group = torch.distributed.group.WORLD
         ctx = ParallelContext(tp_world_size=world, tp_rank=rank, tp_group=group)
@@ -86,8 +89,42 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
                                                  rtol=2e-2))
                 errors.append((m, n, k, call, err, close, nccl_close, tol))
             peer.close()
+        ar_errors = []
+        for (m, n, k) in [(512, 768, 1024), (2048, 3072, 1536)]:
+            peer = PeerAllReduce(ctx, m, n, device)
+            g = torch.Generator().manual_seed(2000 + m)
+            bias = (torch.randn(n, generator=g) * 0.01).to(torch.bfloat16)
+            w_full = orc.weight(n, k, seed=m + 3)
+            kl = k // world
+            w_local = w_full[:, rank * kl:(rank + 1) * kl].contiguous()
+            wq, ws = ops.quantize_weight_int8(w_local.to(device))
+            prev = None
+            for call in range(5):
+                x_full = orc.activation(m, k, seed=call * 11 + m + 1)
+                x_local = x_full[:, rank * kl:(rank + 1) * kl].contiguous()
+                q, s, _ = ops.scaled_int8_quant(x_local.to(device))
+                y = peer(q, s, wq, ws.reshape(-1), bias.to(device))
+                partial = ops.scaled_mm(q, wq.t(), s, ws.reshape(1, -1), torch.bfloat16)
+                nccl = all_reduce_sum(partial, group=group, world_size=world)
+                torch.cuda.synchronize()
+                ref = torch.zeros(m, n, dtype=torch.float32)
+                for r in range(world):
+                    xr = x_full[:, r * kl:(r + 1) * kl]
+                    wr_q, wr_s = orc.quantize_weight(w_full[:, r * kl:(r + 1) * kl])
+                    ref += orc.w8a8_linear(xr, wr_q, wr_s).float()
+                ref = (ref + bias.float()).to(torch.bfloat16).float()
+                got = y.cpu().float()
+                err = float((got - ref).abs().max())
+                close = bool(torch.allclose(got, ref, atol=1e-2, rtol=1e-2))
+                nccl_close = bool(torch.allclose(got, nccl.cpu().float() + bias.float(),
+                                                 atol=2e-2, rtol=2e-2))
+                # the previous call's output is still intact (alternating sets)
+                kept = True if prev is None else bool(torch.equal(prev[0].cpu(), prev[1]))
+                prev = (y, y.cpu().clone())
+                ar_errors.append((m, n, k, call, err, close, nccl_close, kept))
+            peer.close()
         code = ctypes_status(_native)
-        result.update(ok=True, errors=errors, device_status=code)
+        result.update(ok=True, errors=errors, ar_errors=ar_errors, device_status=code)
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
     except Exception:
@@ -127,3 +164,7 @@ def test_fused_reduce_scatter_two_ranks(tmp_path):
         for (m, n, k, call, err, close, nccl_close, tol) in res["errors"]:
             assert close, f"rank {r} {m}x{n}x{k} call {call}: max err {err}"
             assert nccl_close, f"rank {r} {m}x{n}x{k} call {call}: differs from the NCCL path"
+        for (m, n, k, call, err, close, nccl_close, kept) in res["ar_errors"]:
+            assert close, f"all-reduce rank {r} {m}x{n}x{k} call {call}: max err {err}"
+            assert nccl_close, f"all-reduce rank {r} {m}x{n}x{k} call {call}: differs from NCCL"
+            assert kept, f"all-reduce rank {r} {m}x{n}x{k} call {call}: previous output changed"
