@@ -168,6 +168,25 @@ int tm_scaled_mm_i8_splitk_workspace_size(int64_t m, int64_t n, int64_t k, int t
                                           int splits, uint64_t* bytes);
 
 /*
+ * Scaled GEMM with the BF16 LoRA delta added in the epilogue (the reference's
+ * H3InferenceParallelLinearLoRA.forward, src/taomate_hd/inference/
+ * lora_checkpoint.py:126-154: output + bf16(bf16(x A^T) B^T) * scale).
+ * out = epi(dequant(a b^T) (+bias) + lora_t lora_b^T), where lora_t = x A^T
+ * (bf16 [m, r], row stride ldt) and lora_b = scale * B (bf16 [n, r], row
+ * stride ldlb); r = lora_rank in {8, 16, ..., 64}, ldt and ldlb multiples of
+ * 8, both pointers 16-byte aligned.  The update is accumulated in fp32 on the
+ * tensor cores onto the rounded base output and rounded once with it; GELU
+ * (TM_EPI_GELU_TANH) applies to the sum.  Other arguments as
+ * tm_cutlass_scaled_mm.  Runs the 256 x 256 CTA-pair kernel.
+ */
+int tm_scaled_mm_i8_lora(void* out, int out_dtype, const int8_t* a, const int8_t* b,
+                         const float* scale_a, int64_t scale_a_numel, const float* scale_b,
+                         int64_t scale_b_numel, const void* bias, const void* lora_t,
+                         int64_t ldt, const void* lora_b, int64_t ldlb, int lora_rank, int64_t m,
+                         int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldo,
+                         uint32_t epilogue, void* stream);
+
+/*
  * Split-K GEMM that allocates nothing, for callers that cannot call
  * cudaMalloc: code running inside a host process whose device memory is
  * owned and budgeted by someone else (an inference server's pre-partitioned

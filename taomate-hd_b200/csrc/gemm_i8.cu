@@ -1209,6 +1209,375 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (g.world > 0) reduce_phase(g, BN, blockIdx.x, gridDim.x);
 }
 
+// ====================================================================== CTA pair + LoRA
+// The BF16 LoRA delta in the epilogue (the reference's
+// H3InferenceParallelLinearLoRA.forward, lora_checkpoint.py:126-154:
+// output + bf16(bf16(x A^T) B^T) * scale).  T = x A^T ([M, r] bf16, r <= 64)
+// is computed by the caller; B_lora ([N, r] bf16) carries the adapter scale.
+// Per 256 x 256 pair tile, after the int8 main loop:
+//   1. every epilogue warp dequantises its accumulator columns to the
+//      rounded output value y (OutT-rounded, held as fp32) and writes them
+//      back into the same TMEM columns, then signals the leader (conv);
+//   2. the leader's MMA thread adds T_tile * B_lora_tile^T onto them with
+//      four kind::f16 MMAs (K = 64) and commits lora_done to both CTAs;
+//   3. the epilogue reads y + T B^T (fp32), applies GELU if asked, rounds
+//      once and TMA-stores the tile.
+// The accumulator stays 2 x 256 TMEM columns (the 256-wide tile keeps its
+// operand efficiency); T and B_lora tiles use one 32 KiB shared buffer, so
+// the ring has one stage fewer.  The update is added in fp32 and rounded once
+// with y (the reference rounds T B^T to bf16 first): within one bf16 step.
+template <int STAGES>
+struct LoraSmem {
+  static constexpr int kABytes = kBM * kBK;             // 16 KiB
+  static constexpr int kBBytes = 128 * kBK;             // 16 KiB (half of N = 256)
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kLoraOffset = STAGES * kStageBytes;
+  static constexpr int kLoraBytes = 2 * 128 * 128;      // T rows + B_lora rows, 128 B each
+  static constexpr int kBarOffset = kLoraOffset + kLoraBytes;
+  static constexpr int kBarBytes = (2 * STAGES + 10) * 8 + 16;
+  static constexpr int kEpiOffset = (kBarOffset + kBarBytes + 1023) / 1024 * 1024;
+  static constexpr int kTotal = kEpiOffset + kEpiWarps * kEpiStageBytes + 1024;
+  static_assert(kTotal <= 227 * 1024, "shared memory budget");
+};
+
+// Phase 1 of the LoRA epilogue: one warp's 128 columns of int32 accumulator
+// -> rounded output value (fp32 bits) in place.  Constants from the column
+// cache; same arithmetic as dequant16_cached without GELU.
+template <typename OutT>
+__device__ __forceinline__ void lora_convert_in_place(const GemmArgs& g, uint32_t t_row, float sa,
+                                                      const uint8_t* region) {
+  const float* sb_s = reinterpret_cast<const float*>(region + kColCacheOffset);
+  const OutT* bias_s = reinterpret_cast<const OutT*>(region + kBiasCacheOffset);
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c * 32), r);
+    tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float x = __fmul_rn(sb_s[c * 32 + j], __int2float_rn(static_cast<int>(r[j])));
+      const float y = g.bias != nullptr
+                          ? __fmaf_rn(sa, x, out_to_f32<OutT>(bias_s[c * 32 + j]))
+                          : __fmul_rn(sa, x);
+      r[j] = __float_as_uint(round_out<OutT>(y));
+    }
+    tmem_st_32x32b_x32(t_row + static_cast<uint32_t>(c * 32), r);
+  }
+  tmem_st_wait();
+}
+
+// Phase 3: read y + T B^T, GELU if asked, round, stage, TMA store.
+template <typename OutT, typename Release>
+__device__ __forceinline__ void lora_store_tile(const GemmArgs& g, const CUtensorMap* tm_out,
+                                                uint32_t t_row, int64_t row_base, int col_base,
+                                                int lane, uint8_t* region, Release release) {
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c * 32), r);
+    tmem_ld_wait();
+    if (c == 3) release();
+    float y[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      y[j] = __uint_as_float(r[j]);
+      if (g.epilogue & TM_EPI_GELU_TANH) y[j] = gelu_tanh(round_out<OutT>(y[j]));
+    }
+    uint4 o[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      o[q] = make_uint4(pack2<OutT>(y[8 * q], y[8 * q + 1]), pack2<OutT>(y[8 * q + 2], y[8 * q + 3]),
+                        pack2<OutT>(y[8 * q + 4], y[8 * q + 5]),
+                        pack2<OutT>(y[8 * q + 6], y[8 * q + 7]));
+    const int col = col_base + c * 32;
+    if (lane == 0) bulk_wait_read_all();
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < 4; ++q) *stage64_slot(region, lane, q) = o[q];
+    fence_async_shared();
+    __syncwarp();
+    if (lane == 0 && row_base < g.M && col < g.N) {
+      tma_store_2d(tm_out, region, col, static_cast<int>(row_base));
+      bulk_commit();
+    }
+  }
+}
+
+template <int STAGES, typename OutT>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_i8_pair_lora_kernel(const __grid_constant__ CUtensorMap tm_a,
+                             const __grid_constant__ CUtensorMap tm_b,
+                             const __grid_constant__ CUtensorMap tm_out,
+                             const __grid_constant__ CUtensorMap tm_lt,
+                             const __grid_constant__ CUtensorMap tm_lb, const GemmArgs g) {
+  constexpr int BN = 256;
+  constexpr int kBNHalf = BN / 2;
+  using L = LoraSmem<STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1k(smem_raw);
+  uint8_t* s_a = smem;
+  uint8_t* s_b = smem + STAGES * L::kABytes;
+  uint8_t* s_lt = smem + L::kLoraOffset;
+  uint8_t* s_lb = s_lt + 128 * 128;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tmem_full = empty + STAGES;
+  uint64_t* tmem_empty = tmem_full + 2;
+  uint64_t* conv = tmem_empty + 2;       // at the leader: both CTAs' epilogue warps
+  uint64_t* lora_done = conv + 2;        // LoRA MMAs of the accumulator complete
+  uint64_t* lora_full = lora_done + 2;   // T / B_lora tiles landed (leader)
+  uint64_t* lora_empty = lora_full + 1;  // LoRA buffer consumed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(lora_empty + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int tiles = g.num_m * g.num_n;
+  const int pair = blockIdx.x >> 1;
+  const int pairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tmem_full[b], 1);
+      mbar_init(&tmem_empty[b], 2 * kEpiWarps);
+      mbar_init(&conv[b], 2 * kEpiWarps);
+      mbar_init(&lora_done[b], 1);
+    }
+    mbar_init(lora_full, 1);
+    mbar_init(lora_empty, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_a);
+    tma_prefetch_desc(&tm_b);
+    tma_prefetch_desc(&tm_out);
+    tma_prefetch_desc(&tm_lt);
+    tma_prefetch_desc(&tm_lb);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0, lora_phase = 0;
+      uint32_t issued_mask = 0, issued_parity = 0;
+      bool ok = true, lora_inflight = false;
+      const uint32_t lora_full_leader = map_to_cta(smem_u32(lora_full), 0);
+      for (int tile = pair; ok && tile < tiles; tile += pairs) {
+        int mb, nb;
+        tile_coords(tile, g.num_m, g.num_n, mb, nb);
+        const int a_row = mb * 2 * kBM + static_cast<int>(rank) * kBM;
+        const int b_row = nb * BN + static_cast<int>(rank) * kBNHalf;
+        for (int kb = 0; kb < g.kblocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, g.status)) {
+            ok = false;
+            break;
+          }
+          issued_mask &= ~(1u << stage);
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * L::kStageBytes);
+          const uint32_t full_leader = map_to_cta(smem_u32(&full[stage]), 0);
+          tma_load_2d_pair(&tm_a, full_leader, s_a + stage * L::kABytes, kb * kBK, a_row);
+          tma_load_2d_pair(&tm_b, full_leader, s_b + stage * L::kBBytes, kb * kBK, b_row);
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        // this tile's LoRA operands, once the previous tile's LoRA MMAs are done
+        if (!mbar_wait(lora_empty, lora_phase ^ 1u, abort_flag, g.status)) {
+          ok = false;
+          break;
+        }
+        lora_inflight = false;
+        if (leader) mbar_arrive_expect_tx(lora_full, 2 * L::kLoraBytes);
+        tma_load_2d_pair(&tm_lt, lora_full_leader, s_lt, 0, a_row);
+        tma_load_2d_pair(&tm_lb, lora_full_leader, s_lb, 0, b_row);
+        lora_inflight = true;
+        lora_phase ^= 1u;
+      }
+      if (!ok) {
+        if (leader) {
+          for (int s = 0; s < STAGES; ++s)
+            if (issued_mask & (1u << s))
+              mbar_wait_drain(&full[s], (issued_parity >> s) & 1u, g.status);
+          if (lora_inflight) mbar_wait_drain(lora_full, lora_phase ^ 1u, g.status);
+        } else {
+          const uint64_t t0 = globaltimer_ns();
+          while (globaltimer_ns() - t0 < 2000000ull) __nanosleep(1000);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      constexpr uint32_t kIdesc = make_idesc_i8(2 * kBM, BN);
+      constexpr uint32_t kIdescL = make_idesc_bf16(2 * kBM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      uint32_t conv_phase[2] = {0u, 0u};
+      uint32_t lora_phase = 0;
+      int pending = 0;      // tiles whose LoRA MMAs are not issued yet (<= 2)
+      int oldest_acc = 0;   // accumulator of the oldest such tile
+      bool ok = true, issued_any = false;
+      // The LoRA MMAs of the oldest pending tile: wait for its converted
+      // accumulator (both CTAs) and its operand tiles, add T B^T, release.
+      const auto service = [&](bool block) -> bool {
+        const int a = oldest_acc;
+        if (!block && !mbar_test(&conv[a], conv_phase[a])) return true;
+        if (block && !mbar_wait(&conv[a], conv_phase[a], abort_flag, g.status)) return false;
+        if (!mbar_wait(lora_full, lora_phase, abort_flag, g.status)) return false;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(a * BN);
+        const uint32_t lt_addr = smem_u32(s_lt);
+        const uint32_t lb_addr = smem_u32(s_lb);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)  // K = 64 bf16 = 4 x 16
+          umma_bf16_pair(d_tmem, make_desc_kmajor_sw128(lt_addr + k * 32),
+                         make_desc_kmajor_sw128(lb_addr + k * 32), kIdescL, 1u);
+        umma_commit_pair(&lora_done[a], 0x3);
+        umma_commit_pair(lora_empty, 0x3);
+        conv_phase[a] ^= 1u;
+        lora_phase ^= 1u;
+        oldest_acc ^= 1;
+        --pending;
+        return true;
+      };
+      for (int tile = pair; ok && tile < tiles; tile += pairs) {
+        // the accumulator's previous tile must get its LoRA update before
+        // the epilogue can hand the accumulator back
+        if (pending == 2 && !service(true)) {
+          ok = false;
+          break;
+        }
+        if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1u, abort_flag, g.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < g.kblocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, g.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(s_a + stage * L::kABytes);
+          const uint32_t b_addr = smem_u32(s_b + stage * L::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 32; ++k)
+            umma_i8_pair(d_tmem, make_desc_kmajor_sw128(a_addr + k * 32),
+                         make_desc_kmajor_sw128(b_addr + k * 32), kIdesc,
+                         (kb | k) != 0 ? 1u : 0u);
+          issued_any = true;
+          umma_commit_pair(&empty[stage], 0x3);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+          if (pending > 0 && !service(false)) {
+            ok = false;
+            break;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(&tmem_full[acc], 0x3);
+        ++pending;
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      while (ok && pending > 0)
+        if (!service(true)) ok = false;
+      if (!ok && issued_any) {
+        const int last = (stage + STAGES - 1) % STAGES;
+        mbar_wait_drain(&empty[last], stage == 0 ? (phase ^ 1u) : phase, g.status);
+      }
+    }
+    __syncwarp();
+  } else {
+    const uint32_t empty_leader[2] = {map_to_cta(smem_u32(&tmem_empty[0]), 0),
+                                      map_to_cta(smem_u32(&tmem_empty[1]), 0)};
+    const uint32_t conv_leader[2] = {map_to_cta(smem_u32(&conv[0]), 0),
+                                     map_to_cta(smem_u32(&conv[1]), 0)};
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    uint8_t* region = smem + L::kEpiOffset + (warp - 2) * kEpiStageBytes;
+    const int q = warp & 3;
+    const int h = (warp - 2) >> 2;
+    const int epi_row = static_cast<int>(rank) * kBM + q * 32 + lane;
+    ColPrefetch pf{};
+    if (pair < tiles) {
+      int mb0, nb0;
+      tile_coords(pair, g.num_m, g.num_n, mb0, nb0);
+      pf = col_prefetch<OutT>(g, nb0 * BN + h * kBNHalf, kBNHalf,
+                              static_cast<int64_t>(mb0) * 2 * kBM + epi_row, lane);
+    }
+    for (int tile = pair; tile < tiles; tile += pairs) {
+      int mb, nb;
+      tile_coords(tile, g.num_m, g.num_n, mb, nb);
+      col_cache_store(region, pf, kBNHalf, lane);
+      const float sa_tile = pf.sa;
+      __syncwarp();
+      if (tile + pairs < tiles) {
+        int mb1, nb1;
+        tile_coords(tile + pairs, g.num_m, g.num_n, mb1, nb1);
+        pf = col_prefetch<OutT>(g, nb1 * BN + h * kBNHalf, kBNHalf,
+                                static_cast<int64_t>(mb1) * 2 * kBM + epi_row, lane);
+      }
+      if (!mbar_wait(&tmem_full[acc], acc_phase, abort_flag, g.status)) break;
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                             static_cast<uint32_t>(acc * BN + h * kBNHalf);
+      lora_convert_in_place<OutT>(g, t_row, sa_tile, region);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(conv_leader[acc]);
+      if (!mbar_wait(&lora_done[acc], acc_phase, abort_flag, g.status)) break;
+      tc_fence_after();
+      const int64_t row_base = static_cast<int64_t>(mb) * 2 * kBM + rank * kBM + q * 32;
+      const auto release = [&]() {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(empty_leader[acc]);
+      };
+      lora_store_tile<OutT>(g, &tm_out, t_row, row_base, nb * BN + h * kBNHalf, lane, region,
+                            release);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    if (lane == 0) bulk_wait_all();
+  }
+
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, 512);
+  }
+}
+
 // ====================================================================== host
 struct Operands {
   const int8_t* a;
@@ -1302,6 +1671,63 @@ int launch_pair(const Operands& op, GemmArgs args, int max_pairs, cudaStream_t s
   cfg.attrs = attr;
   cfg.numAttrs = args.world > 0 ? 2 : 1;
   if (cudaLaunchKernelEx(&cfg, kernel, ta, tb, to, args) != cudaSuccess) return TM_ERR_CUDA;
+  return check_launch();
+}
+
+// LoRA operands: T = x A^T [M, r] and B_lora [N, r], bf16, r <= 64.
+struct LoraSpec {
+  const void* t;
+  int64_t ldt;
+  const void* b;
+  int64_t ldb;
+  int rank;
+};
+
+template <typename OutT>
+int launch_pair_lora(const Operands& op, GemmArgs args, const LoraSpec& lora, int max_pairs,
+                     cudaStream_t stream) {
+  constexpr int kStages = 5;
+  using L = LoraSmem<kStages>;
+  args.num_m = (args.M + 2 * kBM - 1) / (2 * kBM);
+  args.num_n = (args.N + 255) / 256;
+  args.tma_store = 1;
+  const CUtensorMapDataType dt = std::is_same<OutT, __nv_bfloat16>::value
+                                     ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap ta, tb, to, tlt, tlb;
+  // T and B_lora: r columns, boxes of 64 columns (128 bytes; columns past r
+  // read as zero) x 128 rows
+  if (!encode_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, op.a, args.K, args.M, op.lda, kBK, kBM,
+                      CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, op.b, args.K, args.N, op.ldb, kBK, 128,
+                      CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_tmap_2d(&to, dt, args.out, args.N, args.M, static_cast<uint64_t>(args.ldo) * 2, 32,
+                      32, CU_TENSOR_MAP_SWIZZLE_64B) ||
+      !encode_tmap_2d(&tlt, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, lora.t, lora.rank, args.M,
+                      static_cast<uint64_t>(lora.ldt) * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_tmap_2d(&tlb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, lora.b, lora.rank, args.N,
+                      static_cast<uint64_t>(lora.ldb) * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+    return TM_ERR_CUDA;
+  auto kernel = gemm_i8_pair_lora_kernel<kStages, OutT>;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal) !=
+      cudaSuccess)
+    return TM_ERR_CUDA;
+  const int tiles = args.num_m * args.num_n;
+  const int pairs = tiles < max_pairs ? tiles : max_pairs;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = L::kTotal;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kernel, ta, tb, to, tlt, tlb, args) != cudaSuccess)
+    return TM_ERR_CUDA;
   return check_launch();
 }
 
@@ -1462,7 +1888,8 @@ int scaled_mm_impl(void* out, int out_dtype, const int8_t* a, const int8_t* b, c
                    int64_t sa_numel, const float* sb, int64_t sb_numel, const void* bias,
                    int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldo,
                    uint32_t epilogue, int32_t* acc_debug, int force_cfg, cudaStream_t stream,
-                   const ScatterSpec* scatter = nullptr, const Workspace* ws = nullptr) {
+                   const ScatterSpec* scatter = nullptr, const Workspace* ws = nullptr,
+                   const LoraSpec* lora = nullptr) {
   if (out_dtype != TM_DTYPE_BF16 && out_dtype != TM_DTYPE_FP16) return TM_ERR_DTYPE;
   if (m < 0 || n <= 0 || k <= 0) return TM_ERR_SHAPE;
   if (m > 0x7fffffffLL || n > 0x7fffffffLL || k > 0x7fffffffLL) return TM_ERR_TOO_LARGE;
@@ -1552,6 +1979,14 @@ int scaled_mm_impl(void* out, int out_dtype, const int8_t* a, const int8_t* b, c
     }
   }
   const Operands op{a, lda, b, ldb};
+  if (lora != nullptr) {
+    if (max_pairs <= 0) return TM_ERR_UNSUPPORTED;
+    args.splits = 1;
+    args.kb_per_split = args.kblocks;
+    if (out_dtype == TM_DTYPE_BF16)
+      return launch_pair_lora<__nv_bfloat16>(op, args, *lora, max_pairs, stream);
+    return launch_pair_lora<__half>(op, args, *lora, max_pairs, stream);
+  }
   if (out_dtype == TM_DTYPE_BF16)
     return dispatch<__nv_bfloat16>(op, args, cfg, sms, max_pairs, stream);
   return dispatch<__half>(op, args, cfg, sms, max_pairs, stream);
@@ -1673,6 +2108,24 @@ int tm_scaled_mm_i8_all_reduce(const int8_t* a, const int8_t* b, const float* sc
   return tmw::scaled_mm_impl(own_rows, TM_DTYPE_BF16, a, b, scale_a, scale_a_numel, scale_b,
                              scale_b_numel, bias, m, n, k, lda, ldb, n, 0u, nullptr, tile_n,
                              tmw::as_stream(stream), &spec);
+}
+
+int tm_scaled_mm_i8_lora(void* out, int out_dtype, const int8_t* a, const int8_t* b,
+                         const float* scale_a, int64_t scale_a_numel, const float* scale_b,
+                         int64_t scale_b_numel, const void* bias, const void* lora_t,
+                         int64_t ldt, const void* lora_b, int64_t ldlb, int lora_rank, int64_t m,
+                         int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldo,
+                         uint32_t epilogue, void* stream) {
+  if (lora_rank < 8 || lora_rank > 64 || lora_rank % 8 != 0) return TM_ERR_UNSUPPORTED;
+  if (ldt < lora_rank || ldlb < lora_rank) return TM_ERR_SHAPE;
+  if (ldt % 8 != 0 || ldlb % 8 != 0) return TM_ERR_ALIGNMENT;
+  if (m > 0 && (lora_t == nullptr || lora_b == nullptr)) return TM_ERR_NULL_POINTER;
+  if ((lora_t && !tmw::aligned16(lora_t)) || (lora_b && !tmw::aligned16(lora_b)))
+    return TM_ERR_ALIGNMENT;
+  const tmw::LoraSpec spec{lora_t, ldt, lora_b, ldlb, lora_rank};
+  return tmw::scaled_mm_impl(out, out_dtype, a, b, scale_a, scale_a_numel, scale_b, scale_b_numel,
+                             bias, m, n, k, lda, ldb, ldo, epilogue, nullptr, 0,
+                             tmw::as_stream(stream), nullptr, nullptr, &spec);
 }
 
 int tm_scaled_mm_i8_workspace_size(int64_t m, int64_t n, int64_t k, uint64_t* bytes) {

@@ -208,6 +208,66 @@ void scaled_mm_i8_ex(at::Tensor& out, const at::Tensor& a, const at::Tensor& b,
                    "scaled_mm_i8_ex");
 }
 
+// W8A8 GEMM with the BF16 LoRA delta added in the epilogue:
+// out = epi(dequant(a b) (+bias) + lora_t lora_b^T); lora_t = x A^T [m, r],
+// lora_b = scale * B [n, r], both bf16 with unit inner stride, r <= 64.
+void scaled_mm_i8_lora(at::Tensor& out, const at::Tensor& a, const at::Tensor& b,
+                       const at::Tensor& a_scales, const at::Tensor& b_scales,
+                       const std::optional<at::Tensor>& bias, const at::Tensor& lora_t,
+                       const at::Tensor& lora_b, int64_t epilogue) {
+  check_cuda(a, a, "a");
+  check_cuda(b, a, "b");
+  check_cuda(out, a, "out");
+  check_cuda(a_scales, a, "a_scales");
+  check_cuda(b_scales, a, "b_scales");
+  check_cuda(lora_t, a, "lora_t");
+  check_cuda(lora_b, a, "lora_b");
+  TORCH_CHECK(a.scalar_type() == at::kChar && b.scalar_type() == at::kChar,
+              "a and b must be int8");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && out.dim() == 2, "a, b and out must be 2-D");
+  const int64_t m = a.size(0), k = a.size(1), n = b.size(1);
+  TORCH_CHECK(b.size(0) == k, "a and b inner dimensions differ: ", k, " vs ", b.size(0));
+  TORCH_CHECK(out.size(0) == m && out.size(1) == n, "out must be [", m, ", ", n, "]");
+  TORCH_CHECK(a.stride(1) == 1, "a must be row-major");
+  TORCH_CHECK(b.stride(0) == 1, "b must be column-major (pass weight.t())");
+  TORCH_CHECK(out.stride(1) == 1, "out must be row-major");
+  const int out_dt = dtype_code(out);
+  TORCH_CHECK(out_dt == TM_DTYPE_BF16 || out_dt == TM_DTYPE_FP16, "out must be bfloat16 or float16");
+  TORCH_CHECK(a_scales.scalar_type() == at::kFloat && b_scales.scalar_type() == at::kFloat,
+              "scales must be float32");
+  TORCH_CHECK(a_scales.is_contiguous() && b_scales.is_contiguous(), "scales must be contiguous");
+  TORCH_CHECK(a_scales.numel() == 1 || a_scales.numel() == m, "a_scales must be per-tensor or per-token");
+  TORCH_CHECK(b_scales.numel() == 1 || b_scales.numel() == n, "b_scales must be per-tensor or per-channel");
+  TORCH_CHECK(lora_t.scalar_type() == at::kBFloat16 && lora_b.scalar_type() == at::kBFloat16,
+              "lora_t and lora_b must be bfloat16");
+  TORCH_CHECK(lora_t.dim() == 2 && lora_b.dim() == 2 && lora_t.stride(1) == 1 &&
+                  lora_b.stride(1) == 1,
+              "lora_t and lora_b must be 2-D row-major");
+  const int64_t r = lora_t.size(1);
+  TORCH_CHECK(lora_t.size(0) == m && lora_b.size(0) == n && lora_b.size(1) == r,
+              "lora_t must be [m, r] and lora_b [n, r]");
+  const void* bias_ptr = nullptr;
+  if (bias.has_value()) {
+    check_cuda(*bias, a, "bias");
+    TORCH_CHECK(bias->scalar_type() == out.scalar_type(), "bias must have the output dtype");
+    TORCH_CHECK(bias->numel() == n && bias->is_contiguous(), "bias must be contiguous [n]");
+    bias_ptr = bias->data_ptr();
+  }
+  const int64_t lda = m > 1 ? a.stride(0) : k;
+  const int64_t ldb = n > 1 ? b.stride(1) : k;
+  const int64_t ldo = m > 1 ? out.stride(0) : n;
+  const int64_t ldt = m > 1 ? lora_t.stride(0) : r;
+  const int64_t ldlb = n > 1 ? lora_b.stride(0) : r;
+  const c10::cuda::CUDAGuard guard(a.device());
+  check_status(tm_scaled_mm_i8_lora(out.data_ptr(), out_dt, a.data_ptr<int8_t>(),
+                                    b.data_ptr<int8_t>(), a_scales.data_ptr<float>(),
+                                    a_scales.numel(), b_scales.data_ptr<float>(),
+                                    b_scales.numel(), bias_ptr, lora_t.data_ptr(), ldt,
+                                    lora_b.data_ptr(), ldlb, static_cast<int>(r), m, n, k, lda,
+                                    ldb, ldo, static_cast<uint32_t>(epilogue), stream_of(a)),
+               "scaled_mm_i8_lora");
+}
+
 void quantize_weight_int8(at::Tensor& q, at::Tensor& scales, const at::Tensor& w) {
   check_cuda(w, w, "weight");
   check_cuda(q, w, "q");
@@ -319,6 +379,9 @@ TORCH_LIBRARY(taomate_w8a8, m) {
   m.def(
       "scaled_mm_i8_ex(Tensor(a!) out, Tensor a, Tensor b, Tensor a_scales, Tensor b_scales, "
       "Tensor? bias, int epilogue, Tensor(b!)? acc_debug, int tile_n) -> ()");
+  m.def(
+      "scaled_mm_i8_lora(Tensor(a!) out, Tensor a, Tensor b, Tensor a_scales, Tensor b_scales, "
+      "Tensor? bias, Tensor lora_t, Tensor lora_b, int epilogue) -> ()");
   m.def("quantize_weight_int8(Tensor(a!) q, Tensor(b!) scales, Tensor w) -> ()");
   m.def(
       "modulate_int8_quant(Tensor(a!) out, Tensor(b!) scales, Tensor(c!)? hidden_out, Tensor x, "
@@ -333,6 +396,7 @@ TORCH_LIBRARY_IMPL(taomate_w8a8, CUDA, m) {
   m.impl("static_scaled_int8_quant", &static_scaled_int8_quant);
   m.impl("cutlass_scaled_mm", &cutlass_scaled_mm);
   m.impl("scaled_mm_i8_ex", &scaled_mm_i8_ex);
+  m.impl("scaled_mm_i8_lora", &scaled_mm_i8_lora);
   m.impl("quantize_weight_int8", &quantize_weight_int8);
   m.impl("modulate_int8_quant", &modulate_int8_quant);
   m.impl("rms_norm_modulate_int8_quant", &rms_norm_modulate_int8_quant);

@@ -256,3 +256,157 @@ class TPW8A8BlockChain:
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         h = self.attn.forward(x)
         return self.mlp.forward(h)
+
+
+# ---------------------------------------------------------------- LoRA block stack
+@dataclass
+class LoRAShard:
+    """This rank's LoRA factors: ``a`` bf16 ``[r, K_local]``; ``b`` bf16
+    ``[N_local, r]`` already multiplied by the adapter scale alpha / r."""
+
+    a: torch.Tensor
+    b: torch.Tensor
+
+
+def column_lora(n: int, k: int, rank: int, alpha: float, ctx: ParallelContext, seed: int,
+                device: torch.device, output_sizes: tuple[int, ...] | None = None) -> LoRAShard:
+    """Column LoRA shards (lora_checkpoint.py:73-88): full A, B sharded per projection."""
+    a = random_bf16((rank, k), 0.02, seed, device)
+    b_full = random_bf16((n, rank), 0.002, seed + 1, device)
+    t, r = ctx.tp_world_size, ctx.tp_rank
+    pieces, offset = [], 0
+    for size in output_sizes or (n,):
+        local = size // t
+        pieces.append(b_full.narrow(0, offset + r * local, local))
+        offset += size
+    b = (torch.cat(pieces, 0).float() * (alpha / rank)).to(torch.bfloat16).contiguous()
+    return LoRAShard(a, b)
+
+
+def row_lora(n: int, k: int, rank: int, alpha: float, ctx: ParallelContext, seed: int,
+             device: torch.device) -> LoRAShard:
+    """Row LoRA shards (lora_checkpoint.py:91-97): A sliced along K, full B."""
+    a_full = random_bf16((rank, k), 0.02, seed, device)
+    t, r = ctx.tp_world_size, ctx.tp_rank
+    a = a_full.narrow(1, r * (k // t), k // t).contiguous()
+    b = (random_bf16((n, rank), 0.002, seed + 1, device).float() * (alpha / rank)).to(torch.bfloat16)
+    return LoRAShard(a, b.contiguous())
+
+
+@dataclass
+class _BlockWeights:
+    qkv: W8Weight
+    qkv_lora: LoRAShard
+    out: W8Weight
+    out_lora: LoRAShard
+    fc1: W8Weight
+    fc1_lora: LoRAShard
+    fc2: W8Weight
+    fc2_lora: LoRAShard
+
+
+class TPW8A8LoRABlockStack:
+    """``n_blocks`` chained 768p DiT block linear chains.
+
+    Per block: adaLN modulate (per-token shift/scale) fused into the
+    activation quant -> merged QKV (+bias, LoRA) -> out-projection of the
+    attention output (the Q shard stands in for attention, which is outside
+    the W8A8 path) (+bias, LoRA) and its row reduction -> modulate fused into
+    the quant -> fc1 (+bias, LoRA, GELU-tanh) -> quant -> fc2 (+bias, LoRA)
+    and its row reduction.  Every W8A8 linear adds its BF16 LoRA delta
+    (rank 64, alpha 64) in the GEMM epilogue; the LoRA down-projection
+    T = x A^T is a plain bf16 GEMM.  Row-parallel linears follow the
+    reference's fused-row-reduce LoRA (lora_checkpoint.py:127-143):
+    reduce(partial + update) + bias, with the bias on TP rank 0 and an NCCL
+    all-reduce.  Each block has its own random weights; activation buffers
+    are shared by all blocks, so a forward allocates nothing.
+    """
+
+    def __init__(self, n_blocks: int, tokens: int, d: int, heads: int, head_dim: int, ffn: int,
+                 ctx: ParallelContext, device: torch.device, *, rank: int = 64,
+                 alpha: float = 64.0, seed: int = 0):
+        t = ctx.tp_world_size
+        width = heads * head_dim
+        if heads % t or ffn % t:
+            raise ValueError("heads and ffn must divide by the TP degree")
+        self.ctx, self.tokens, self.d, self.width, self.ffn = ctx, tokens, d, width, ffn
+        self.rank = rank
+        self.blocks: list[_BlockWeights] = []
+        for i in range(n_blocks):
+            s = seed + 1000 * i
+            sizes = (width, width, width)
+            self.blocks.append(_BlockWeights(
+                qkv=column_weight(3 * width, d, ctx, s + 30, device, bias=True, output_sizes=sizes),
+                qkv_lora=column_lora(3 * width, d, rank, alpha, ctx, s + 35, device, sizes),
+                out=row_weight(d, width, ctx, s + 40, device, bias=True),
+                out_lora=row_lora(d, width, rank, alpha, ctx, s + 45, device),
+                fc1=column_weight(ffn, d, ctx, s + 50, device, bias=True),
+                fc1_lora=column_lora(ffn, d, rank, alpha, ctx, s + 55, device),
+                fc2=row_weight(d, ffn, ctx, s + 60, device, bias=True),
+                fc2_lora=row_lora(d, ffn, rank, alpha, ctx, s + 65, device)))
+        # adaLN shift/scale, per token, shared by the blocks
+        self.shift1 = random_bf16((tokens, d), 0.1, seed + 1, device)
+        self.scale1 = random_bf16((tokens, d), 0.1, seed + 2, device)
+        self.shift2 = random_bf16((tokens, d), 0.1, seed + 3, device)
+        self.scale2 = random_bf16((tokens, d), 0.1, seed + 4, device)
+        bf = dict(dtype=torch.bfloat16, device=device)
+        self.q_in = _Quant(tokens, d, device)
+        self.hidden = torch.empty(tokens, d, **bf)
+        self.t_buf = torch.empty(tokens, rank, **bf)
+        self.qkv_out = torch.empty(tokens, 3 * width // t, **bf)
+        self.q_attn = _Quant(tokens, width // t, device)
+        self.attn_out = torch.empty(tokens, d, **bf)
+        self.h = torch.empty(tokens, ffn // t, **bf)
+        self.q2 = _Quant(tokens, ffn // t, device)
+        self.y = [torch.empty(tokens, d, **bf) for _ in range(2)]
+
+    @property
+    def int8_ops_per_block(self) -> int:
+        """Whole-job int8 GEMM operations of one block (2 M N K per linear)."""
+        m, d, w, f = self.tokens, self.d, self.width, self.ffn
+        return 2 * m * (d * 3 * w + w * d + d * f + f * d)
+
+    @property
+    def lora_flops_per_block(self) -> int:
+        """Whole-job bf16 LoRA flops of one block: 2 M r (K + N) per linear."""
+        m, d, w, f, r = self.tokens, self.d, self.width, self.ffn, self.rank
+        return 2 * m * r * ((d + 3 * w) + (w + d) + (d + f) + (f + d))
+
+    # this package's kernel launches per block: 2 modulate-quant + 2 quant + 4
+    # LoRA GEMMs (plus 4 bf16 LoRA down-projections on cuBLAS)
+    launches_per_block = 8
+
+    def _lora_linear(self, q: _Quant, w: W8Weight, lora: LoRAShard, x: torch.Tensor,
+                     out: torch.Tensor, bias: torch.Tensor | None, gelu: bool = False) -> None:
+        torch.mm(x, lora.a.t(), out=self.t_buf)
+        torch.ops.taomate_w8a8.scaled_mm_i8_lora(out, q.q, w.q_t, q.s, w.scale, bias, self.t_buf,
+                                                 lora.b, ops.EPI_GELU_TANH if gelu else 0)
+
+    def _reduce(self, y: torch.Tensor) -> torch.Tensor:
+        t = self.ctx.tp_world_size
+        if t == 1:
+            return y
+        return all_reduce_sum_inplace_(y, group=self.ctx.tp_group, world_size=t)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        t, first = self.ctx.tp_world_size, self.ctx.tp_rank == 0
+        for i, blk in enumerate(self.blocks):
+            torch.ops.taomate_w8a8.modulate_int8_quant(self.q_in.q, self.q_in.s, self.hidden, x,
+                                                       self.shift1, self.scale1, None)
+            self._lora_linear(self.q_in, blk.qkv, blk.qkv_lora, self.hidden, self.qkv_out,
+                              blk.qkv.bias)
+            attn = self.qkv_out[:, : self.width // t]
+            self.q_attn(attn)
+            self._lora_linear(self.q_attn, blk.out, blk.out_lora, attn, self.attn_out,
+                              blk.out.bias if first else None)
+            a = self._reduce(self.attn_out)
+            torch.ops.taomate_w8a8.modulate_int8_quant(self.q_in.q, self.q_in.s, self.hidden, a,
+                                                       self.shift2, self.scale2, None)
+            self._lora_linear(self.q_in, blk.fc1, blk.fc1_lora, self.hidden, self.h, blk.fc1.bias,
+                              gelu=True)
+            self.q2(self.h)
+            y = self.y[i % 2]
+            self._lora_linear(self.q2, blk.fc2, blk.fc2_lora, self.h, y,
+                              blk.fc2.bias if first else None)
+            x = self._reduce(y)
+        return x

@@ -115,6 +115,36 @@ def scaled_mm(
     return out
 
 
+def scaled_mm_lora(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    scale_a: torch.Tensor,
+    scale_b: torch.Tensor,
+    lora_t: torch.Tensor,
+    lora_b: torch.Tensor,
+    out_dtype: torch.dtype = torch.bfloat16,
+    bias: torch.Tensor | None = None,
+    *,
+    gelu_tanh: bool = False,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """:func:`scaled_mm` plus a BF16 LoRA delta added in the epilogue.
+
+    ``lora_t`` is ``x A^T`` (bf16 ``[M, r]``, r <= 64, a multiple of 8) and
+    ``lora_b`` the adapter's B already multiplied by its scale (bf16
+    ``[N, r]``); the result is ``epi(dequant(a b) (+bias) + lora_t lora_b^T)``
+    with the update added in fp32 and rounded once together with the base
+    output (GELU, when asked, applies to the sum).
+    """
+    _require_cuda(a, b, scale_a, scale_b, bias, out, lora_t, lora_b)
+    a2 = a.reshape(-1, a.shape[-1])
+    if out is None:
+        out = torch.empty((a2.shape[0], b.shape[1]), dtype=out_dtype, device=a.device)
+    _ops.scaled_mm_i8_lora(out, a2, b, scale_a, scale_b, bias, lora_t, lora_b,
+                           EPI_GELU_TANH if gelu_tanh else 0)
+    return out
+
+
 def quantize_weight_int8(weight: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """Per-output-channel symmetric int8 weight conversion on the GPU.
 
