@@ -241,6 +241,48 @@ def run_reference(args) -> int:
 
 
 # ----------------------------------------------------------------- our arm
+STACK_BLOCKS = 40
+
+
+def lora_block_stack(ctx, device: torch.device, g: torch.Generator, world: int,
+                     flush: torch.Tensor) -> dict:
+    """40 chained 768p blocks (QKV, out-proj, fc1, fc2) with
+    the BF16 LoRA (rank 64, alpha 64) in the W8A8 epilogue and adaLN modulate
+    fused into the activation quant; each block has its own weights, so every
+    block streams its weights from HBM.  One forward of the 40 blocks per
+    timed repetition (L2 flushed before it)."""
+    from taomate_hd_b200.dit import TPW8A8LoRABlockStack
+
+    stack = TPW8A8LoRABlockStack(STACK_BLOCKS, BLOCK_TOKENS, D, HEADS, HEAD_DIM, FFN, ctx, device,
+                                 seed=11)
+    x = torch.randn(BLOCK_TOKENS, D, generator=g, device=device).to(torch.bfloat16)
+    stack.forward(x)
+    torch.cuda.synchronize()
+    barrier(world)
+    reps = 3
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(reps)]
+    for e0, e1 in ev:
+        flush.zero_()
+        e0.record()
+        stack.forward(x)
+        e1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(sum(e0.elapsed_time(e1) for e0, e1 in ev) / reps, world, device)
+    per_block = ms / STACK_BLOCKS
+    out = {"blocks": STACK_BLOCKS, "ms_per_forward": ms, "ms_per_block": per_block,
+           "int8_tops": stack.int8_ops_per_block / (per_block * 1e-3) / 1e12,
+           "lora_bf16_tflops": stack.lora_flops_per_block / (per_block * 1e-3) / 1e12,
+           "config": f"M={BLOCK_TOKENS}, d={D}, heads {HEADS}x{HEAD_DIM}, ffn {FFN}, LoRA rank "
+                     f"{stack.rank} alpha 64 in every W8A8 epilogue, per-token adaLN modulate fused "
+                     "into the quant, GELU-tanh after fc1; row-parallel reduce: "
+                     + ("none (TP=1)" if world == 1 else "NCCL all-reduce"),
+           "gpu_launches_per_block": stack.launches_per_block}
+    del stack
+    return out
+
+
 SWEEP_M = (64, 256, 1024, 4096, 16384, 32768)
 SWEEP_NK = ((3072, 3072), (12288, 3072))  # (N, K)
 
@@ -276,7 +318,7 @@ def skinny_sweep(world: int, device: torch.device, flush: torch.Tensor) -> list[
                   for _ in range(reps)]
             for e0, e1 in ev:
                 flush.zero_()
-                torch.sum(clean, out=sink)
+                torch.sum(clean, dim=0, out=sink)
                 e0.record()
                 ops.scaled_mm(a, w.t(), sa, sb, torch.bfloat16)
                 e1.record()
@@ -356,10 +398,14 @@ def run_ours(args) -> int:
     # (host->device on one, device->host on another) into double-buffered device
     # staging, so step i's read-back and step i+1's upload overlap the kernels as
     # in a serving loop; the region spans all K steps and ends when the last
-    # read-back has landed.
-    x_host = x.cpu().pin_memory()
+    # read-back has landed.  With N ranks each uploads its 1/N row slice of the
+    # input and the ranks all-gather it over NVLink (NCCL) before the forward,
+    # so the host link carries the input once per step in total.
+    rows_in = TOKENS // world
+    x_host = x[rank * rows_in:(rank + 1) * rows_in].cpu().pin_memory()
     out_rows = mlp.out.shape[0] if world > 1 else TOKENS
     x_dev = [torch.empty_like(x) for _ in range(2)]
+    x_part = [torch.empty(rows_in, D, dtype=x.dtype, device=device) for _ in range(2)]
     y_dev = [torch.empty(out_rows, D, dtype=torch.bfloat16, device=device) for _ in range(2)]
     y_host = [torch.empty(out_rows, D, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
     main = torch.cuda.current_stream(device)
@@ -373,10 +419,12 @@ def run_ours(args) -> int:
         b = i % 2
         with torch.cuda.stream(up):
             up.wait_event(x_free[b])
-            x_dev[b].copy_(x_host, non_blocking=True)
+            (x_part[b] if world > 1 else x_dev[b]).copy_(x_host, non_blocking=True)
             x_ready[b].record(up)
         flush.zero_()
         main.wait_event(x_ready[b])
+        if world > 1:
+            torch.distributed.all_gather_into_tensor(x_dev[b], x_part[b])
         y = mlp.forward(x_dev[b])
         x_free[b].record(main)
         main.wait_event(y_free[b])
@@ -427,12 +475,15 @@ def run_ours(args) -> int:
         block_ops = block.int8_ops
         del block
         torch.cuda.empty_cache()
+        lora_stack = lora_block_stack(ctx, device, g, world, flush)
+        torch.cuda.empty_cache()
         sweep = skinny_sweep(world, device, flush)
         extras = {"ms_per_768p_block_linear_chain": block_ms,
                   "block_768p_tops": block_ops / (block_ms * 1e-3) / 1e12,
                   "block_768p_config": f"M={BLOCK_TOKENS}, d={D}, QKV N={3 * HEADS * HEAD_DIM}, "
                                        f"out-proj, fc1 N={FFN} (+GELU), fc2; all-reduce after "
                                        f"row-parallel linears; no LoRA / modulate fusion",
+                  "lora_block_stack_768p": lora_stack,
                   "skinny_sweep": sweep}
 
     if rank == 0:
@@ -472,10 +523,11 @@ def run_ours(args) -> int:
                 "kernel": "fc2 scatter-mode GEMM + owner reduction (partials leaving each rank)"},
             "e2e": {"value": total_ops / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS",
                     "ms_per_step": e2e_ms,
-                    "h2d_bytes_per_step": world * x.numel() * x.element_size(),
+                    "h2d_bytes_per_step": world * x_host.numel() * x_host.element_size(),
                     "d2h_bytes_per_step": world * y_host[0].numel() * y_host[0].element_size(),
                     "pipelining": "upload and read-back on their own streams, double-buffered; "
-                                  "L2 flushed inside the region before each step"},
+                                  "L2 flushed inside the region before each step; N > 1: each "
+                                  "rank uploads its row slice, NCCL all-gather of the input"},
             "gpu_launches": K * launches,
             "wall_s_timed_region": wall,
             "extras": extras,
