@@ -69,10 +69,14 @@ def sat_round_int8(v: np.ndarray) -> np.ndarray:
 def dynamic_scaled_int8_quant(x: torch.Tensor | np.ndarray) -> tuple[np.ndarray, np.ndarray]:
     """Per-token dynamic symmetric int8 quant (vLLM op called at w8a8.py:71).
 
-    Returns ``(q int8 [rows, K], scales float32 [rows])``.
+    Returns ``(q int8 [rows, K], scales float32 [rows])``.  NaN elements do not
+    enter the row maximum and quantise to 0; infinities saturate.
     """
     xf = to_f32(x).reshape(-1, np.shape(x)[-1])
-    amax = np.max(np.abs(xf), axis=1).astype(F32) if xf.shape[1] else np.zeros(xf.shape[0], F32)
+    # row maximum of |x| from 0 with NaN elements left out (an fmax
+    # reduction; NaN handling is not pinned by golden vectors)
+    amax = (np.fmax.reduce(np.abs(xf), axis=1, initial=F32(0.0)).astype(F32)
+            if xf.shape[1] else np.zeros(xf.shape[0], F32))
     scales = (amax / F32(127.0)).astype(F32)
     with np.errstate(divide="ignore"):
         inv = np.where(amax == 0, F32(0.0), F32(127.0) / amax).astype(F32)

@@ -76,6 +76,21 @@ __device__ __forceinline__ int f2i8_rn_sat(float x) {
   return r;
 }
 
+// The same value as f2i8_rn_sat for x in [-127.5, 127.5] or NaN, on the FP32
+// pipe: NaN becomes 0, then adding 1.5 * 2^23 makes the addition's
+// round-to-nearest-even leave round(x) in the low mantissa bits; the low byte
+// of the result is the two's-complement int8 (the bits of 1.5 * 2^23 are
+// 0x4B400000).
+__device__ __forceinline__ uint32_t f2i8_rn_fast(float x) {
+  return __float_as_uint(__fadd_rn(x == x ? x : 0.0f, 12582912.0f));
+}
+
+// Pack the low bytes of four words into one.
+__device__ __forceinline__ uint32_t pack_low_bytes(uint32_t b0, uint32_t b1, uint32_t b2,
+                                                   uint32_t b3) {
+  return __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
+}
+
 template <typename T>
 struct VecTraits {
   static constexpr int kElems = 16 / sizeof(T);
@@ -127,6 +142,45 @@ __device__ __forceinline__ float group_reduce(float v, int tpr, float* red) {
     v = acc;
   }
   return v;
+}
+
+// Quantise a thread's VPT vectors of E values and store them.  kFast: the
+// FP32-pipe rounding (dynamic modes, rows where it equals the conversion);
+// chosen per row outside the loop so each path is straight-line code.
+template <int MODE, bool kFast, int VPT, int E>
+__device__ __forceinline__ void store_q(const float (&v)[VPT][E], int8_t* qr, int t, int tpr,
+                                        int64_t nvec, float inv, float static_s) {
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int64_t vi = t + static_cast<int64_t>(i) * tpr;
+    if (vi < nvec) {
+      uint32_t packed[E / 4];
+#pragma unroll
+      for (int w = 0; w < E / 4; ++w) {
+        uint32_t bytes[4];
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          const float xv = v[i][4 * w + b];
+          if constexpr (MODE == kStatic) {
+            bytes[b] = static_cast<uint32_t>(f2i8_rn_sat(__fdiv_rn(xv, static_s)));
+          } else if constexpr (MODE == kWeight) {
+            const int qi = f2i8_rn_sat(__fdiv_rn(xv, inv));
+            bytes[b] = static_cast<uint32_t>(qi < -127 ? -127 : qi);
+          } else if constexpr (kFast) {
+            bytes[b] = f2i8_rn_fast(__fmul_rn(xv, inv));
+          } else {
+            bytes[b] = static_cast<uint32_t>(f2i8_rn_sat(__fmul_rn(xv, inv)));
+          }
+        }
+        packed[w] = pack_low_bytes(bytes[0], bytes[1], bytes[2], bytes[3]);
+      }
+      if constexpr (E == 8) {
+        *reinterpret_cast<uint2*>(qr + vi * E) = make_uint2(packed[0], packed[1]);
+      } else {
+        *reinterpret_cast<uint32_t*>(qr + vi * E) = packed[0];
+      }
+    }
+  }
 }
 
 template <typename T, int VPT, int MODE>
@@ -204,6 +258,12 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const QuantParams p) {
   }
 
   float inv;
+  // dynamic modes: with a finite row maximum (NaN elements do not enter it)
+  // and a finite 127 / amax every x * inv of a finite x rounds into
+  // [-127, 127] (|x| <= amax), and NaN elements give NaN, so the FP32-pipe
+  // rounding gives the conversion's result; other rows (an infinite element,
+  // or a subnormal maximum) keep the conversion instruction
+  bool fast = false;
   if constexpr (MODE == kStatic) {
     inv = 0.f;  // unused: static mode divides by the given scale
   } else {
@@ -220,42 +280,19 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const QuantParams p) {
     } else {
       if (active && t == 0) p.scales[row] = __fdiv_rn(amax, 127.0f);
       inv = amax == 0.f ? 0.f : __fdiv_rn(127.0f, amax);
+      fast = isfinite(amax) && isfinite(inv);
     }
   }
   const float static_s = MODE == kStatic ? *p.static_scale : 0.f;
 
   if (!active) return;
   int8_t* qr = p.q + row * p.cols;
-#pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    const int64_t vi = t + static_cast<int64_t>(i) * tpr;
-    if (vi < nvec) {
-      uint32_t packed[E / 4];
-#pragma unroll
-      for (int w = 0; w < E / 4; ++w) {
-        uint32_t word = 0;
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-          const float xv = v[i][4 * w + b];
-          int qi;
-          if constexpr (MODE == kStatic) {
-            qi = f2i8_rn_sat(__fdiv_rn(xv, static_s));
-          } else if constexpr (MODE == kWeight) {
-            qi = f2i8_rn_sat(__fdiv_rn(xv, inv));
-            qi = qi < -127 ? -127 : qi;
-          } else {
-            qi = f2i8_rn_sat(__fmul_rn(xv, inv));
-          }
-          word |= (static_cast<uint32_t>(qi) & 0xffu) << (8 * b);
-        }
-        packed[w] = word;
-      }
-      if constexpr (E == 8) {
-        *reinterpret_cast<uint2*>(qr + vi * E) = make_uint2(packed[0], packed[1]);
-      } else {
-        *reinterpret_cast<uint32_t*>(qr + vi * E) = packed[0];
-      }
-    }
+  if constexpr (MODE == kStatic || MODE == kWeight) {
+    store_q<MODE, false>(v, qr, t, tpr, nvec, inv, static_s);
+  } else if (fast) {
+    store_q<MODE, true>(v, qr, t, tpr, nvec, inv, static_s);
+  } else {
+    store_q<MODE, false>(v, qr, t, tpr, nvec, inv, static_s);
   }
 }
 

@@ -57,6 +57,25 @@ def test_dynamic_quant_edge_rows(tm_ops, cuda):
     assert q[1, 3].item() == -127
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_dynamic_quant_non_finite_rows(tm_ops, cuda, dtype):
+    """Rows whose maximum is inf, NaN or subnormal (127 / amax overflows) take
+    the conversion-instruction path; finite rows the FP32-pipe rounding: both
+    bit-exact with the oracle (NaN -> 0, saturation at -128 / 127)."""
+    x = torch.randn(8, 1024) * 3
+    x[0, 5] = float("inf")
+    x[1, 7] = float("-inf")
+    x[2, 9] = float("nan")
+    x[3] = 0.0
+    x[3, :4] = torch.tensor([1e-40, -2e-40, 3e-41, 0.0])  # subnormal row maximum
+    x[4, 11] = 1e30  # large but finite
+    xd = x.to(dtype)
+    q, s, _ = tm_ops.scaled_int8_quant(xd.to(cuda))
+    q_ref, s_ref = orc.dynamic_scaled_int8_quant(xd)
+    np.testing.assert_array_equal(q.cpu().numpy(), q_ref)
+    np.testing.assert_array_equal(s.cpu().numpy().reshape(-1), s_ref)
+
+
 def test_dynamic_quant_3d_and_strided(tm_ops, cuda):
     x = _rand(6 * 5, 768, torch.bfloat16, seed=5).reshape(6, 5, 768).to(cuda)
     q, s, _ = tm_ops.scaled_int8_quant(x)
