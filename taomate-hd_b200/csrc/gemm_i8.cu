@@ -1252,14 +1252,32 @@ __device__ __forceinline__ void lora_convert_in_place(const GemmArgs& g, uint32_
   for (int c = 0; c < 4; ++c) {
     uint32_t r[32];
     tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c * 32), r);
-    tmem_ld_wait();
+    float sb[32];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const float x = __fmul_rn(sb_s[c * 32 + j], __int2float_rn(static_cast<int>(r[j])));
-      const float y = g.bias != nullptr
-                          ? __fmaf_rn(sa, x, out_to_f32<OutT>(bias_s[c * 32 + j]))
-                          : __fmul_rn(sa, x);
-      r[j] = __float_as_uint(round_out<OutT>(y));
+    for (int j = 0; j < 8; ++j) {
+      const float4 v = reinterpret_cast<const float4*>(sb_s + c * 32)[j];
+      sb[4 * j] = v.x;
+      sb[4 * j + 1] = v.y;
+      sb[4 * j + 2] = v.z;
+      sb[4 * j + 3] = v.w;
+    }
+    tmem_ld_wait();
+    if (g.bias != nullptr) {
+      uint4 braw[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) braw[j] = reinterpret_cast<const uint4*>(bias_s + c * 32)[j];
+      const OutT* be = reinterpret_cast<const OutT*>(braw);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float x = __fmul_rn(sb[j], __int2float_rn(static_cast<int>(r[j])));
+        r[j] = __float_as_uint(round_out<OutT>(__fmaf_rn(sa, x, out_to_f32<OutT>(be[j]))));
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float x = __fmul_rn(sb[j], __int2float_rn(static_cast<int>(r[j])));
+        r[j] = __float_as_uint(round_out<OutT>(__fmul_rn(sa, x)));
+      }
     }
     tmem_st_32x32b_x32(t_row + static_cast<uint32_t>(c * 32), r);
   }
