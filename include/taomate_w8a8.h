@@ -142,9 +142,9 @@ int tm_scaled_mm_i8_tile(void* out, int out_dtype, const int8_t* a, const int8_t
  * caller-provided workspace; when the shape leaves most SMs idle (small M)
  * it cuts K into slices computed by separate CTAs, which store exact int32
  * partials in the workspace; the last slice of each tile to finish sums them
- * and runs the epilogue (results are identical to the unsplit GEMM).  The
- * workspace must be 16-byte aligned and zeroed before its first use; every
- * complete call leaves its counters at zero again.  Calls that share a
+ * and runs the epilogue (results are identical to the unsplit GEMM).  The workspace (a 64 KiB counter region,
+ * then the partials) must be 16-byte aligned and zeroed before its first use;
+ * every complete call leaves its counters at zero again.  Calls that share a
  * workspace must not overlap on the GPU.  With workspace_bytes smaller than
  * tm_scaled_mm_i8_workspace_size(m, n, k) the call runs unsplit.
  * tm_scaled_mm_i8_splitk forces a one-CTA tile width (256/128/64) and a
@@ -196,7 +196,7 @@ int tm_scaled_mm_i8_lora(void* out, int out_dtype, const int8_t* a, const int8_t
  * without the workspace and acc_debug: the int32 partials live in a
  * TM_SPLITK_NOALLOC_MAX_BYTES (16 MiB) array compiled into the library,
  * which every GPU that loads the library holds until the process exits.
- * Requests whose split needs more than that (tile counters plus
+ * Requests whose split needs more than that (a 64 KiB counter region plus
  * splits x m x n x 4 bytes) fail with TM_ERR_TOO_LARGE.  The first call on a
  * device looks up the array's device address (cudaGetSymbolAddress), so make
  * that first call before any stream capture.  Every call shares the one

@@ -110,11 +110,15 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int&
 }
 
 __device__ __forceinline__ float gelu_tanh(float x) {
-  // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))
-  const float k_beta = 0.7978845608028654f;
-  const float k_kappa = 0.044715f;
-  const float inner = k_beta * fmaf(k_kappa * x * x, x, x);
-  return 0.5f * x * (1.0f + tanh_approx(inner));
+  // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))), every operation explicit
+  // (no contraction left to the compiler), so each epilogue path that
+  // inlines it computes the same bits
+  // inner = x (beta + beta kappa x^2); result = 0.5 x + 0.5 x tanh(inner)
+  const float k_beta = 0.7978845608028654f;          // sqrt(2 / pi)
+  const float k_beta_kappa = 0.035677408136300125f;  // sqrt(2 / pi) * 0.044715
+  const float inner = __fmul_rn(x, __fmaf_rn(k_beta_kappa, __fmul_rn(x, x), k_beta));
+  const float h = __fmul_rn(0.5f, x);
+  return __fmaf_rn(h, tanh_approx(inner), h);
 }
 
 template <typename OutT>
@@ -1830,6 +1834,13 @@ Choice pick_choice(int m, int n, int kblocks, int sms, int max_pairs, bool allow
 
 // Effective slice count (no empty slice) and workspace bytes of a split-K
 // run: per-tile counters (256-byte aligned) followed by `splits` int32 [M, N].
+// Split-K workspaces start with a fixed counter region: the counters reset
+// themselves to zero at the end of every call, and the int32 partials always
+// start after the region, so a call's partials can never land on the
+// counters of a later call with more tiles (a workspace is zeroed once and
+// reused).
+constexpr uint64_t kCounterRegion = 64 * 1024;
+
 struct SplitPlan {
   int splits;
   int kb_per_split;
@@ -1849,7 +1860,11 @@ SplitPlan plan_split(int cfg, int splits, int m, int n, int kblocks) {
     return p;
   }
   const uint64_t tiles = static_cast<uint64_t>((m + kBM - 1) / kBM) * ((n + bn - 1) / bn);
-  p.counter_bytes = (tiles * 4 + 255) / 256 * 256;
+  p.counter_bytes = kCounterRegion;
+  if (tiles * 4 > kCounterRegion) {  // more tiles than counters: no workspace can hold it
+    p.bytes = ~0ull;
+    return p;
+  }
   p.bytes = p.counter_bytes + static_cast<uint64_t>(p.splits) * m * n * 4;
   return p;
 }

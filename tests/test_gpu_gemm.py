@@ -192,3 +192,17 @@ def test_skinny_m_heuristic_path(tm_ops, cuda, capi, m, n, k):
         np.testing.assert_array_equal(acc, acc_ref)
         ref = orc.scaled_mm_epilogue(acc_ref, sa.numpy(), sb.numpy(), bias, torch.bfloat16, gelu=gelu)
         torch.testing.assert_close(out.float(), ref.float(), atol=ATOL, rtol=RTOL)
+
+
+def test_split_workspace_reuse_with_more_tiles(tm_ops, cuda):
+    """Two split-K calls through the torch op's cached workspace, the second
+    with more tiles (48 then 72 one-CTA tiles of 64 columns): the second call's
+    counters must not start on the first call's partials.  Bit-exact with the
+    unsplit kernel."""
+    for (m, n, k) in [(16, 3072, 12288), (128, 4608, 12288)]:
+        a, b, sa, sb, bias = _operands(m, n, k, seed=m + n, bias_dtype=torch.bfloat16)
+        a_d, b_d, sa_d, sb_d, bias_d = (t.to(cuda) for t in (a, b, sa, sb, bias))
+        split = tm_ops.scaled_mm(a_d, b_d.t(), sa_d, sb_d, torch.bfloat16, bias_d)
+        whole = tm_ops.scaled_mm(a_d, b_d.t(), sa_d, sb_d, torch.bfloat16, bias_d, tile_n=64)
+        torch.cuda.synchronize()
+        torch.testing.assert_close(split, whole, atol=0, rtol=0)
