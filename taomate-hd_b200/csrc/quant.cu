@@ -17,6 +17,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <type_traits>
+
 #include "common.h"
 
 namespace tmw {
@@ -194,6 +196,70 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const QuantParams p) {
   const bool active = row < p.rows;
   const int64_t nvec = p.cols / E;
   const T* xr = reinterpret_cast<const T*>(p.x) + (active ? row : 0) * p.ldx;
+
+  if constexpr (MODE == kDynamic && std::is_same<T, __nv_bfloat16>::value) {
+    // Plain dynamic quant of bf16: the row maximum from packed bf16 pairs
+    // (|x| and max are exact in bf16, and equal the fp32 maximum of the
+    // converted values; NaN elements are left out as by fmaxf), a second
+    // NaN-propagating packed maximum flags rows with NaN, and only the
+    // multiply-and-round runs per element in fp32.  Rows with NaN, inf or a
+    // subnormal maximum take the conversion instruction.
+    uint4 raw[VPT];
+    __nv_bfloat162 m2 = __float2bfloat162_rn(0.0f), n2 = m2;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int64_t vi = t + static_cast<int64_t>(i) * tpr;
+      raw[i] = (active && vi < nvec) ? ld_stream16(xr + vi * E) : make_uint4(0u, 0u, 0u, 0u);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[i]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const __nv_bfloat162 a = __habs2(h[j]);
+        m2 = __hmax2(m2, a);
+        n2 = __hmax2_nan(n2, a);
+      }
+    }
+    float amax = fmaxf(__bfloat162float(m2.x), __bfloat162float(m2.y));
+    float has_nan = (__hisnan(n2.x) || __hisnan(n2.y)) ? 1.0f : 0.0f;
+    amax = group_reduce<true>(amax, tpr, red);
+    has_nan = group_reduce<true>(has_nan, tpr, red);
+    if (!active) return;
+    if (t == 0) p.scales[row] = __fdiv_rn(amax, 127.0f);
+    const float inv = amax == 0.f ? 0.f : __fdiv_rn(127.0f, amax);
+    const bool fast = has_nan == 0.0f && isfinite(amax) && isfinite(inv);
+    int8_t* qr = p.q + row * p.cols;
+    // one straight-line store loop per rounding path, chosen once per row
+    const auto store_row = [&](auto fast_tag) {
+      constexpr bool kFast = decltype(fast_tag)::value;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int64_t vi = t + static_cast<int64_t>(i) * tpr;
+        if (vi < nvec) {
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[i]);
+          uint32_t bytes[8];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = __bfloat1622float2(h[j]);
+            const float y0 = __fmul_rn(f.x, inv), y1 = __fmul_rn(f.y, inv);
+            if constexpr (kFast) {  // no NaN / inf here: |y| rounds into [-127, 127]
+              bytes[2 * j] = __float_as_uint(__fadd_rn(y0, 12582912.0f));
+              bytes[2 * j + 1] = __float_as_uint(__fadd_rn(y1, 12582912.0f));
+            } else {
+              bytes[2 * j] = static_cast<uint32_t>(f2i8_rn_sat(y0));
+              bytes[2 * j + 1] = static_cast<uint32_t>(f2i8_rn_sat(y1));
+            }
+          }
+          *reinterpret_cast<uint2*>(qr + vi * E) =
+              make_uint2(pack_low_bytes(bytes[0], bytes[1], bytes[2], bytes[3]),
+                         pack_low_bytes(bytes[4], bytes[5], bytes[6], bytes[7]));
+        }
+      }
+    };
+    if (fast)
+      store_row(std::true_type{});
+    else
+      store_row(std::false_type{});
+    return;
+  }
 
   float v[VPT][E];
 #pragma unroll
