@@ -48,6 +48,16 @@ extern "C" {
 /* ---- GEMM epilogue flags (tm_scaled_mm_i8_ex) -------------------------- */
 /* gelu_tanh applied to the rounded output: y = round(gelu(round(x)))      */
 #define TM_EPI_GELU_TANH 0x1u
+/*
+ * SwiGLU after a merged gate/up projection (the reference's fused_swiglu,
+ * src/taomate_hd/inference/fused_kernels.py:298-309, after the merged fc1,
+ * model/layers.py:525-533): the weight's n rows (and scales, bias) come
+ * interleaved in blocks of 16 -- 16 gate rows, then the 16 matching up rows
+ * -- and the output has n / 2 columns, out = round(round(g * sigmoid(g)) * u)
+ * with g, u the rounded linear outputs.  n % 64 == 0; not combined with
+ * GELU, the fused reductions or LoRA.
+ */
+#define TM_EPI_SWIGLU 0x2u
 
 /* Human-readable text for a status code (static storage). */
 const char* tm_status_string(int status);

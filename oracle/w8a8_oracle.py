@@ -177,6 +177,19 @@ def gelu_tanh(x: torch.Tensor) -> torch.Tensor:
     return torch.nn.functional.gelu(x.to(torch.float32), approximate="tanh").to(x.dtype)
 
 
+def swiglu(value: torch.Tensor) -> torch.Tensor:
+    """``fused_swiglu`` (fused_kernels.py:298-309, 694-704): gate, up = halves;
+    ``round_bf16(round_bf16(gate * sigmoid(gate)) * up)`` in fp32."""
+    v = to_f32(value).reshape(-1, value.shape[-1])
+    half = v.shape[1] // 2
+    gate, up = v[:, :half], v[:, half:]
+    with np.errstate(over="ignore"):
+        sig = (F32(1.0) / (F32(1.0) + np.exp(-gate).astype(F32))).astype(F32)
+    act = round_bf16((gate * sig).astype(F32))
+    out = round_bf16((act * up).astype(F32))
+    return torch.from_numpy(out).to(torch.bfloat16).reshape(*value.shape[:-1], half)
+
+
 # ---------------------------------------------------------------- adaLN producers
 def modulate(
     x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, index: torch.Tensor | None = None

@@ -89,6 +89,18 @@ def build_capi(verbose: bool = False) -> Path:
     return CAPI_SO
 
 
+def _cxx() -> str:
+    """The host C++ compiler for the torch op library: the system ``g++`` on
+    PATH (torch's own toolchain), not ``$CXX``.  A compiler that links
+    libstdc++ statically would give the library a private copy of the iostream
+    and locale machinery, and the first error message formatted inside an op
+    (TORCH_CHECK with a number) would crash instead of raising."""
+    cxx = shutil.which("g++")
+    if cxx is None:
+        raise RuntimeError("g++ not found on PATH")
+    return cxx
+
+
 def build_torch_ops(verbose: bool = False) -> Path:
     import torch
     from torch.utils import cpp_extension
@@ -100,7 +112,7 @@ def build_torch_ops(verbose: bool = False) -> Path:
     abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
     tmp = TORCH_SO.with_suffix(".so.tmp")
     cmd = [
-        os.environ.get("CXX", "g++"), "-O2", "-std=c++17", "-fPIC", "-shared",
+        _cxx(), "-O2", "-std=c++17", "-fPIC", "-shared",
         f"-D_GLIBCXX_USE_CXX11_ABI={abi}", *includes,
         *(str(CSRC / s) for s in TORCH_SOURCES),
         "-o", str(tmp),
@@ -109,8 +121,16 @@ def build_torch_ops(verbose: bool = False) -> Path:
         "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{torch_lib}",
     ]
     _run(cmd, verbose)
+    _require_shared_libstdcxx(tmp)
     os.replace(tmp, TORCH_SO)
     return TORCH_SO
+
+
+def _require_shared_libstdcxx(path: Path) -> None:
+    """Refuse a torch op library that does not load the shared libstdc++."""
+    needed = subprocess.run(["readelf", "-d", str(path)], capture_output=True, text=True)
+    if needed.returncode == 0 and "libstdc++.so" not in needed.stdout:
+        raise RuntimeError(f"{path.name} does not link libstdc++ dynamically; check the C++ compiler")
 
 
 def build(force: bool = False, verbose: bool = False) -> None:

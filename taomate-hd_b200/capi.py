@@ -30,6 +30,7 @@ TM_DTYPE_FP16 = 1
 TM_DTYPE_FP32 = 2
 
 TM_EPI_GELU_TANH = 0x1
+TM_EPI_SWIGLU = 0x2
 TM_SPLITK_NOALLOC_MAX_BYTES = 16 << 20
 
 _GEMM = [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_i64, c_void_p, c_i64, c_void_p,

@@ -455,6 +455,81 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmArgs& g, const CUten
   }
 }
 
+// SwiGLU epilogue (TM_EPI_SWIGLU, the reference's fused_swiglu after the
+// merged fc1, fused_kernels.py:298-309 and model/layers.py:525-533).  The
+// weight rows arrive interleaved in blocks of 16 -- gate rows j..j+15, then
+// the matching up rows -- so every 32 accumulator columns hold 16 (gate, up)
+// pairs.  Per 64-column pass: dequantise both halves to the rounded linear
+// output (as the unfused linear would store them), then
+// out = round(round(g * sigmoid(g)) * u) for 32 output columns, staged and
+// TMA-stored at output column (acc column) / 2.  `release` as in
+// epilogue_tile_tma.
+__device__ __forceinline__ float sigmoid_f32(float x) {
+  return __fdividef(1.0f, __fadd_rn(1.0f, __expf(-x)));
+}
+
+template <int BN, typename OutT, typename Release>
+__device__ __forceinline__ void epilogue_tile_swiglu(const GemmArgs& g, const CUtensorMap* tm_out,
+                                                     uint32_t tmem_base, uint32_t acc_col,
+                                                     int64_t row0, int col0, int warp, int lane,
+                                                     uint8_t* region, float sa, Release release) {
+  constexpr int kHalf = BN / 2;
+  constexpr int kPasses = kHalf / 64;
+  static_assert(kHalf % 64 == 0 && kHalf <= 128, "64-column passes, cache of 128 columns");
+  const int q = warp & 3;
+  const int h = (warp - 2) >> 2;
+  const int64_t row_base = row0 + q * 32;
+  const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc_col +
+                         static_cast<uint32_t>(h * kHalf);
+  const float* sb_s = reinterpret_cast<const float*>(region + kColCacheOffset);
+  const OutT* bias_s = reinterpret_cast<const OutT*>(region + kBiasCacheOffset);
+#pragma unroll 1
+  for (int pass = 0; pass < kPasses; ++pass) {
+    uint32_t r[2][32];
+    tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(pass * 64), r[0]);
+    tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(pass * 64 + 32), r[1]);
+    tmem_ld_wait();
+    if (pass == kPasses - 1) release();
+    float out[32];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int cc = pass * 64 + k * 32;  // cache column of this 32-column chunk
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        float y[2];
+#pragma unroll
+        for (int part = 0; part < 2; ++part) {  // 0: gate column, 1: up column
+          const int c = cc + part * 16 + j;
+          const float x = __fmul_rn(sb_s[c], __int2float_rn(static_cast<int>(r[k][part * 16 + j])));
+          const float v = g.bias != nullptr ? __fmaf_rn(sa, x, out_to_f32<OutT>(bias_s[c]))
+                                            : __fmul_rn(sa, x);
+          y[part] = round_out<OutT>(v);
+        }
+        const float act = round_out<OutT>(__fmul_rn(y[0], sigmoid_f32(y[0])));
+        out[k * 16 + j] = __fmul_rn(act, y[1]);
+      }
+    }
+    uint4 o[4];
+#pragma unroll
+    for (int qd = 0; qd < 4; ++qd)
+      o[qd] = make_uint4(pack2<OutT>(out[8 * qd], out[8 * qd + 1]),
+                         pack2<OutT>(out[8 * qd + 2], out[8 * qd + 3]),
+                         pack2<OutT>(out[8 * qd + 4], out[8 * qd + 5]),
+                         pack2<OutT>(out[8 * qd + 6], out[8 * qd + 7]));
+    const int out_col = (col0 + h * kHalf + pass * 64) / 2;
+    if (lane == 0) bulk_wait_read_all();
+    __syncwarp();
+#pragma unroll
+    for (int qd = 0; qd < 4; ++qd) *stage64_slot(region, lane, qd) = o[qd];
+    fence_async_shared();
+    __syncwarp();
+    if (lane == 0 && row_base < g.M && 2 * out_col < g.N) {
+      tma_store_2d(tm_out, region, out_col, static_cast<int>(row_base));
+      bulk_commit();
+    }
+  }
+}
+
 // Fused reduce-scatter: after a CTA's epilogue warps have issued the stores
 // of all their blocks, one thread drains them (the named barrier orders
 // every warp's stores before that thread's system-scope fence; fences are
@@ -968,9 +1043,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (g.splits > 1) {
         release();
       } else if (g.tma_store) {
-        epilogue_tile_tma<BN, OutT>(g, &tm_out, tmem_base, static_cast<uint32_t>(acc * BN),
-                                    static_cast<int64_t>(mb) * kBM, nb * BN, warp, lane, stage,
-                                    sa_tile, release);
+        bool done = false;
+        if constexpr ((BN / 2) % 64 == 0) {
+          if (g.epilogue & TM_EPI_SWIGLU) {
+            epilogue_tile_swiglu<BN, OutT>(g, &tm_out, tmem_base, static_cast<uint32_t>(acc * BN),
+                                           static_cast<int64_t>(mb) * kBM, nb * BN, warp, lane,
+                                           stage, sa_tile, release);
+            done = true;
+          }
+        }
+        if (!done)
+          epilogue_tile_tma<BN, OutT>(g, &tm_out, tmem_base, static_cast<uint32_t>(acc * BN),
+                                      static_cast<int64_t>(mb) * kBM, nb * BN, warp, lane, stage,
+                                      sa_tile, release);
       } else {
         epilogue_tile<BN, OutT>(g, tmem_base, static_cast<uint32_t>(acc * BN),
                                 static_cast<int64_t>(mb) * kBM, nb * BN, warp, lane, stage);
@@ -1186,8 +1271,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive_cluster(acc == 0 ? empty_leader0 : empty_leader1);
       };
       if (g.tma_store) {
-        epilogue_tile_tma<BN, OutT>(g, &tm_out, tmem_base, static_cast<uint32_t>(acc * BN), row0,
-                                    nb * BN, warp, lane, stage, sa_tile, release);
+        bool done = false;
+        if constexpr ((BN / 2) % 64 == 0) {
+          if (g.epilogue & TM_EPI_SWIGLU) {
+            epilogue_tile_swiglu<BN, OutT>(g, &tm_out, tmem_base, static_cast<uint32_t>(acc * BN),
+                                           row0, nb * BN, warp, lane, stage, sa_tile, release);
+            done = true;
+          }
+        }
+        if (!done)
+          epilogue_tile_tma<BN, OutT>(g, &tm_out, tmem_base, static_cast<uint32_t>(acc * BN),
+                                      row0, nb * BN, warp, lane, stage, sa_tile, release);
       } else {
         epilogue_tile<BN, OutT>(g, tmem_base, static_cast<uint32_t>(acc * BN), row0, nb * BN, warp,
                                 lane, stage);
@@ -1619,8 +1713,10 @@ bool encode_out_map(CUtensorMap* map, GemmArgs& args) {
   const CUtensorMapDataType dt = std::is_same<OutT, __nv_bfloat16>::value
                                      ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  return encode_tmap_2d(map, dt, args.out, args.N, args.M, static_cast<uint64_t>(args.ldo) * 2, 32,
-                        32, CU_TENSOR_MAP_SWIZZLE_64B);
+  // SwiGLU writes N / 2 output columns
+  const uint64_t out_cols = (args.epilogue & TM_EPI_SWIGLU) ? args.N / 2 : args.N;
+  return encode_tmap_2d(map, dt, args.out, out_cols, args.M, static_cast<uint64_t>(args.ldo) * 2,
+                        32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
 }
 
 template <int BN, int STAGES, typename OutT>
@@ -1927,11 +2023,18 @@ int scaled_mm_impl(void* out, int out_dtype, const int8_t* a, const int8_t* b, c
   if (m < 0 || n <= 0 || k <= 0) return TM_ERR_SHAPE;
   if (m > 0x7fffffffLL || n > 0x7fffffffLL || k > 0x7fffffffLL) return TM_ERR_TOO_LARGE;
   if (k % 16 != 0 || n % 16 != 0) return TM_ERR_SHAPE;
-  if (lda < k || ldb < k || ldo < n) return TM_ERR_SHAPE;
+  const bool swiglu = (epilogue & TM_EPI_SWIGLU) != 0;
+  // SwiGLU: n interleaved (gate, up) columns in, n / 2 columns out
+  if (lda < k || ldb < k || ldo < (swiglu ? n / 2 : n)) return TM_ERR_SHAPE;
   if (lda % 16 != 0 || ldb % 16 != 0 || ldo % 8 != 0) return TM_ERR_ALIGNMENT;
   if (sa_numel != 1 && sa_numel != m) return TM_ERR_SHAPE;
   if (sb_numel != 1 && sb_numel != n) return TM_ERR_SHAPE;
-  if (epilogue & ~TM_EPI_GELU_TANH) return TM_ERR_UNSUPPORTED;
+  if (epilogue & ~(TM_EPI_GELU_TANH | TM_EPI_SWIGLU)) return TM_ERR_UNSUPPORTED;
+  if (swiglu) {
+    if (epilogue & TM_EPI_GELU_TANH) return TM_ERR_UNSUPPORTED;
+    if (n % 64 != 0) return TM_ERR_SHAPE;
+    if (scatter != nullptr || lora != nullptr) return TM_ERR_UNSUPPORTED;
+  }
   if (scatter != nullptr) {
     if (scatter->world < 1 || scatter->world > kMaxPeers) return TM_ERR_TOO_LARGE;
     if (scatter->rank < 0 || scatter->rank >= scatter->world) return TM_ERR_SHAPE;
@@ -1988,10 +2091,16 @@ int scaled_mm_impl(void* out, int out_dtype, const int8_t* a, const int8_t* b, c
     }
   }
   const int max_pairs = max_resident_pairs(dev, sms);
-  const bool can_split = ws != nullptr && ws->ptr != nullptr && scatter == nullptr;
+  const bool can_split = ws != nullptr && ws->ptr != nullptr && scatter == nullptr && !swiglu;
   Choice choice = pick_choice(args.M, args.N, args.kblocks, sms, max_pairs, can_split);
   if (force_cfg) choice = Choice{force_cfg, 1};
   if (can_split && ws->force_splits > 0) choice.splits = ws->force_splits;
+  if (swiglu) {
+    // the SwiGLU epilogue works in 64-column passes of each warp's half tile
+    if (choice.cfg == 64) choice.cfg = 128;
+    if (choice.cfg == kPairFlag + 192) choice.cfg = kPairFlag + 256;
+    choice.splits = 1;
+  }
   const int cfg = choice.cfg;
   if (cfg > kPairFlag && max_pairs <= 0) return TM_ERR_UNSUPPORTED;
   args.splits = 1;

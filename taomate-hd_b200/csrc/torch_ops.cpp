@@ -134,7 +134,9 @@ void scaled_mm_common(at::Tensor& out, const at::Tensor& a, const at::Tensor& b,
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && out.dim() == 2, "a, b and out must be 2-D");
   const int64_t m = a.size(0), k = a.size(1), n = b.size(1);
   TORCH_CHECK(b.size(0) == k, "a and b inner dimensions differ: ", k, " vs ", b.size(0));
-  TORCH_CHECK(out.size(0) == m && out.size(1) == n, "out must be [", m, ", ", n, "]");
+  // SwiGLU: n interleaved (gate, up) columns in, n / 2 out
+  const int64_t out_n = (epilogue & TM_EPI_SWIGLU) ? n / 2 : n;
+  TORCH_CHECK(out.size(0) == m && out.size(1) == out_n, "out must be [", m, ", ", out_n, "]");
   TORCH_CHECK(a.stride(1) == 1, "a must be row-major");
   TORCH_CHECK(b.stride(0) == 1, "b must be column-major (pass weight.t())");
   TORCH_CHECK(out.stride(1) == 1, "out must be row-major");
@@ -162,7 +164,7 @@ void scaled_mm_common(at::Tensor& out, const at::Tensor& a, const at::Tensor& b,
   }
   const int64_t lda = m > 1 ? a.stride(0) : k;
   const int64_t ldb = n > 1 ? b.stride(1) : k;
-  const int64_t ldo = m > 1 ? out.stride(0) : n;
+  const int64_t ldo = m > 1 ? out.stride(0) : out_n;
   const c10::cuda::CUDAGuard guard(a.device());
   int status;
   if (tile_n != 0) {

@@ -20,6 +20,7 @@ load_torch_ops()
 _ops = torch.ops.taomate_w8a8
 
 EPI_GELU_TANH = 0x1
+EPI_SWIGLU = 0x2
 
 
 def _require_cuda(*tensors: torch.Tensor | None) -> None:
@@ -95,6 +96,7 @@ def scaled_mm(
     bias: torch.Tensor | None = None,
     *,
     gelu_tanh: bool = False,
+    swiglu: bool = False,
     out: torch.Tensor | None = None,
     acc_debug: torch.Tensor | None = None,
     tile_n: int = 0,
@@ -102,17 +104,37 @@ def scaled_mm(
     """:func:`cutlass_scaled_mm` with the fused epilogue options.
 
     ``gelu_tanh`` applies ``round(gelu_tanh(round(y)))`` to the dequantised
-    (+bias) output; ``acc_debug`` (int32 ``[M, N]``) receives the raw
+    (+bias) output.  ``swiglu`` expects ``b``'s N columns as interleaved
+    (gate, up) blocks (:func:`interleave_gate_up`) and returns ``[M, N / 2]``
+    ``round(round(g * sigmoid(g)) * u)`` (the reference's fused_swiglu after
+    the merged fc1).  ``acc_debug`` (int32 ``[M, N]``) receives the raw
     accumulators; ``out`` makes the call allocation-free; ``tile_n`` forces
     the N-tile width (0 = heuristic).
     """
     _require_cuda(a, b, scale_a, scale_b, bias, out, acc_debug)
+    if gelu_tanh and swiglu:
+        raise ValueError("gelu_tanh and swiglu are exclusive")
     a2 = a.reshape(-1, a.shape[-1])
     if out is None:
-        out = torch.empty((a2.shape[0], b.shape[1]), dtype=out_dtype, device=a.device)
-    _ops.scaled_mm_i8_ex(out, a2, b, scale_a, scale_b, bias,
-                         EPI_GELU_TANH if gelu_tanh else 0, acc_debug, tile_n)
+        cols = b.shape[1] // 2 if swiglu else b.shape[1]
+        out = torch.empty((a2.shape[0], cols), dtype=out_dtype, device=a.device)
+    epi = (EPI_GELU_TANH if gelu_tanh else 0) | (EPI_SWIGLU if swiglu else 0)
+    _ops.scaled_mm_i8_ex(out, a2, b, scale_a, scale_b, bias, epi, acc_debug, tile_n)
     return out
+
+
+def interleave_gate_up(t: torch.Tensor, block: int = 16) -> torch.Tensor:
+    """Reorder a merged ``[gate; up]`` tensor (rows, or a 1-D vector) into the
+    SwiGLU epilogue's layout: ``block`` gate rows, then the matching ``block``
+    up rows, repeated.  Per-row quantisation commutes with the reordering, so
+    int8 weights and their scales can be interleaved before or after it."""
+    rows = t.shape[0]
+    if rows % (2 * block):
+        raise ValueError(f"rows ({rows}) must be a multiple of {2 * block}")
+    half = rows // 2
+    gate = t[:half].reshape(half // block, block, *t.shape[1:])
+    up = t[half:].reshape(half // block, block, *t.shape[1:])
+    return torch.stack((gate, up), dim=1).reshape(t.shape).contiguous()
 
 
 def scaled_mm_lora(

@@ -173,6 +173,26 @@ def test_build_is_current():
     assert native_build.is_current(), "run `python -m taomate_hd_b200.build`"
 
 
+def test_torch_op_library_links_shared_libstdcxx():
+    """The op library must use the process's libstdc++: a statically linked
+    copy has its own locale state and crashes while formatting the first
+    error message an op raises."""
+    import shutil
+    import subprocess
+
+    from taomate_hd_b200 import build
+
+    if shutil.which("readelf") is None:
+        pytest.skip("readelf not available")
+    dyn = subprocess.run(["readelf", "-d", str(build.TORCH_SO)], capture_output=True, text=True)
+    assert dyn.returncode == 0
+    assert "libstdc++.so" in dyn.stdout
+    syms = subprocess.run(["readelf", "--dyn-syms", "--wide", str(build.TORCH_SO)],
+                          capture_output=True, text=True).stdout
+    assert "_ZNSo9_M_insertIlEERSoT_" not in [line.split()[-1] for line in syms.splitlines()
+                                               if " DEFAULT " in line and " UND " not in line]
+
+
 def test_c_abi_exports_every_header_symbol():
     lib = ctypes.CDLL(str(native_build.CAPI_SO))
     names = capi_mod.header_symbols()
