@@ -197,6 +197,22 @@ int tm_scaled_mm_i8_lora(void* out, int out_dtype, const int8_t* a, const int8_t
                          uint32_t epilogue, void* stream);
 
 /*
+ * Merged QKV projection written straight into the Ulysses all-to-all send
+ * layout (the reference's merged_qkv_sequence_to_heads builds it with a
+ * permute copy, src/taomate_hd/distributed/ulysses.py:153-212): the GEMM of
+ * tm_cutlass_scaled_mm with n = 3 x num_heads x head_dim, whose epilogue
+ * stores row r, column (qkv, head, d) at send[w][qkv][r][(head % lh) *
+ * head_dim + d], w = head / lh, lh = num_heads / world; `send` is a
+ * contiguous [world][3][m][lh x head_dim] buffer to pass to the all-to-all.
+ * num_heads % world == 0, head_dim % 32 == 0, m % 32 == 0.
+ */
+int tm_scaled_mm_i8_ulysses_send(void* send, int out_dtype, const int8_t* a, const int8_t* b,
+                                 const float* scale_a, int64_t scale_a_numel,
+                                 const float* scale_b, int64_t scale_b_numel, const void* bias,
+                                 int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
+                                 int num_heads, int head_dim, int world, void* stream);
+
+/*
  * Split-K GEMM that allocates nothing, for callers that cannot call
  * cudaMalloc: code running inside a host process whose device memory is
  * owned and budgeted by someone else (an inference server's pre-partitioned

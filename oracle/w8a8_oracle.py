@@ -236,6 +236,16 @@ def lora_column(
     return base_out + update * scale
 
 
+def merged_qkv_send_layout(value: torch.Tensor, num_heads: int, head_dim: int,
+                           world: int) -> torch.Tensor:
+    """``_merged_qkv_send_layout`` (distributed/ulysses.py:153-163):
+    ``[tokens, 3 * heads * head_dim]`` -> ``[world, 3, tokens, heads / world, head_dim]``."""
+    tokens = value.shape[0]
+    local = num_heads // world
+    return (value.view(tokens, 3, num_heads, head_dim).view(tokens, 3, world, local, head_dim)
+            .permute(2, 1, 0, 3, 4).contiguous())
+
+
 # ---------------------------------------------------------------- TP sharding
 def column_shard(full: torch.Tensor, tp_size: int, tp_rank: int) -> torch.Tensor:
     """``ColumnParallelLinear.full_weight_slice`` (linear.py:161-166)."""

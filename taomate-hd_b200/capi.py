@@ -66,6 +66,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_i64, c_void_p, c_i64, c_void_p,
                 c_void_p, c_i64, c_void_p, c_i64, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
                 c_u32, c_void_p]),
+    "tm_scaled_mm_i8_ulysses_send": (
+        c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_i64, c_void_p, c_i64, c_void_p,
+                c_i64, c_i64, c_i64, c_i64, c_i64, c_int, c_int, c_int, c_void_p]),
     "tm_scaled_mm_i8_splitk_noalloc": (c_int, [*_GEMM, c_u32, c_int, c_int, c_void_p]),
     "tm_peer_handle_size": (c_int, []),
     "tm_peer_alloc": (c_int, [ctypes.c_uint64, ctypes.POINTER(c_void_p), c_void_p]),

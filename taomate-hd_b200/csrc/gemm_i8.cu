@@ -65,6 +65,12 @@ struct GemmArgs {
   // tm_out map) instead of per-lane stores; set only without split-K or
   // scatter.
   int tma_store;
+  // Ulysses send layout (ul_world > 0; merged QKV projection, n = 3 x heads
+  // x head_dim): the output is the all-to-all send buffer
+  // [ul_world][3][M][heads / ul_world x head_dim] (the reference's
+  // _merged_qkv_send_layout, distributed/ulysses.py:153-163) instead of
+  // [M][N]; see ulysses_coords.
+  int ul_world, ul_heads, ul_head_dim;
   // Split-K (one-CTA kernel): each tile's K range is cut into `splits`
   // slices of kb_per_split k-blocks; every (tile, slice) unit stores its exact
   // int32 partial in ws[slice][M][N] and bumps tile_counters[tile]; the unit
@@ -317,6 +323,24 @@ __device__ __forceinline__ uint4* stage64_slot(uint8_t* stage, int row, int chun
   return reinterpret_cast<uint4*>(stage + row * 64 + ((chunk ^ ((row >> 1) & 3)) << 4));
 }
 
+// Ulysses send layout: output column `col` (a multiple of 32, never crossing
+// a head) of row `row` goes to the send buffer viewed as
+// [ul_world * 3 * M rows][heads / ul_world * head_dim columns]: row
+// (w * 3 + qkv) * M + row, column (head % local_heads) * head_dim + d, with
+// qkv = col / (heads * head_dim), head = that part / head_dim and
+// w = head / local_heads.
+__device__ __forceinline__ void ulysses_coords(const GemmArgs& g, int col, int64_t row, int& x,
+                                               int64_t& y) {
+  const int width = g.ul_heads * g.ul_head_dim;
+  const int qkv = col / width;
+  const int within = col - qkv * width;
+  const int head = within / g.ul_head_dim;
+  const int local_heads = g.ul_heads / g.ul_world;
+  const int w = head / local_heads;
+  x = within - w * local_heads * g.ul_head_dim;
+  y = static_cast<int64_t>(w * 3 + qkv) * g.M + row;
+}
+
 // One lane's share of a tile's column constants: 4 scales, 4 bias values,
 // and the per-token scale of its row.
 struct ColPrefetch {
@@ -449,7 +473,10 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmArgs& g, const CUten
     fence_async_shared();
     __syncwarp();
     if (lane == 0 && row_base < g.M && col < g.N) {
-      tma_store_2d(tm_out, region, col, static_cast<int>(row_base));
+      int x = col;
+      int64_t y = row_base;
+      if (g.ul_world > 0) ulysses_coords(g, col, row_base, x, y);
+      tma_store_2d(tm_out, region, x, static_cast<int>(y));
       bulk_commit();
     }
   }
@@ -1713,6 +1740,11 @@ bool encode_out_map(CUtensorMap* map, GemmArgs& args) {
   const CUtensorMapDataType dt = std::is_same<OutT, __nv_bfloat16>::value
                                      ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  if (args.ul_world > 0) {  // send buffer as [world * 3 * M][local heads x head_dim]
+    const uint64_t cols = static_cast<uint64_t>(args.ul_heads / args.ul_world) * args.ul_head_dim;
+    return encode_tmap_2d(map, dt, args.out, cols, static_cast<uint64_t>(3) * args.ul_world * args.M,
+                          cols * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+  }
   // SwiGLU writes N / 2 output columns
   const uint64_t out_cols = (args.epilogue & TM_EPI_SWIGLU) ? args.N / 2 : args.N;
   return encode_tmap_2d(map, dt, args.out, out_cols, args.M, static_cast<uint64_t>(args.ldo) * 2,
@@ -2005,6 +2037,11 @@ struct ScatterSpec {
   void* const* peer_out = nullptr;  // all-reduce: every rank's [M][N] output
 };
 
+// Ulysses send layout of a merged QKV projection.
+struct UlyssesSpec {
+  int heads, head_dim, world;
+};
+
 // Optional split-K workspace (zeroed by the caller before its first use; the
 // kernel leaves its counters at zero again after every complete call).
 struct Workspace {
@@ -2018,12 +2055,20 @@ int scaled_mm_impl(void* out, int out_dtype, const int8_t* a, const int8_t* b, c
                    int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldo,
                    uint32_t epilogue, int32_t* acc_debug, int force_cfg, cudaStream_t stream,
                    const ScatterSpec* scatter = nullptr, const Workspace* ws = nullptr,
-                   const LoraSpec* lora = nullptr) {
+                   const LoraSpec* lora = nullptr, const UlyssesSpec* ul = nullptr) {
   if (out_dtype != TM_DTYPE_BF16 && out_dtype != TM_DTYPE_FP16) return TM_ERR_DTYPE;
   if (m < 0 || n <= 0 || k <= 0) return TM_ERR_SHAPE;
   if (m > 0x7fffffffLL || n > 0x7fffffffLL || k > 0x7fffffffLL) return TM_ERR_TOO_LARGE;
   if (k % 16 != 0 || n % 16 != 0) return TM_ERR_SHAPE;
   const bool swiglu = (epilogue & TM_EPI_SWIGLU) != 0;
+  if (ul != nullptr) {
+    if (ul->world < 1 || ul->heads < 1 || ul->heads % ul->world != 0) return TM_ERR_SHAPE;
+    if (ul->head_dim % 32 != 0 || n != 3LL * ul->heads * ul->head_dim) return TM_ERR_SHAPE;
+    if (m % 32 != 0) return TM_ERR_SHAPE;  // a 32-row store box never crosses a group
+    if (3LL * ul->world * m > 0x7fffffffLL) return TM_ERR_TOO_LARGE;
+    if (swiglu || scatter != nullptr || lora != nullptr) return TM_ERR_UNSUPPORTED;
+    ldo = n;  // the row-stride checks below see a [m, n] output; the layout is the send buffer
+  }
   // SwiGLU: n interleaved (gate, up) columns in, n / 2 columns out
   if (lda < k || ldb < k || ldo < (swiglu ? n / 2 : n)) return TM_ERR_SHAPE;
   if (lda % 16 != 0 || ldb % 16 != 0 || ldo % 8 != 0) return TM_ERR_ALIGNMENT;
@@ -2075,6 +2120,11 @@ int scaled_mm_impl(void* out, int out_dtype, const int8_t* a, const int8_t* b, c
   args.epilogue = epilogue;
   args.status = device_status_ptr(dev);
   if (args.status == nullptr) return TM_ERR_CUDA;
+  if (ul != nullptr) {
+    args.ul_world = ul->world;
+    args.ul_heads = ul->heads;
+    args.ul_head_dim = ul->head_dim;
+  }
   if (scatter != nullptr) {
     args.world = scatter->world;
     args.rank = scatter->rank;
@@ -2091,7 +2141,8 @@ int scaled_mm_impl(void* out, int out_dtype, const int8_t* a, const int8_t* b, c
     }
   }
   const int max_pairs = max_resident_pairs(dev, sms);
-  const bool can_split = ws != nullptr && ws->ptr != nullptr && scatter == nullptr && !swiglu;
+  const bool can_split =
+      ws != nullptr && ws->ptr != nullptr && scatter == nullptr && !swiglu && ul == nullptr;
   Choice choice = pick_choice(args.M, args.N, args.kblocks, sms, max_pairs, can_split);
   if (force_cfg) choice = Choice{force_cfg, 1};
   if (can_split && ws->force_splits > 0) choice.splits = ws->force_splits;
@@ -2268,6 +2319,17 @@ int tm_scaled_mm_i8_lora(void* out, int out_dtype, const int8_t* a, const int8_t
   return tmw::scaled_mm_impl(out, out_dtype, a, b, scale_a, scale_a_numel, scale_b, scale_b_numel,
                              bias, m, n, k, lda, ldb, ldo, epilogue, nullptr, 0,
                              tmw::as_stream(stream), nullptr, nullptr, &spec);
+}
+
+int tm_scaled_mm_i8_ulysses_send(void* send, int out_dtype, const int8_t* a, const int8_t* b,
+                                 const float* scale_a, int64_t scale_a_numel,
+                                 const float* scale_b, int64_t scale_b_numel, const void* bias,
+                                 int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
+                                 int num_heads, int head_dim, int world, void* stream) {
+  const tmw::UlyssesSpec spec{num_heads, head_dim, world};
+  return tmw::scaled_mm_impl(send, out_dtype, a, b, scale_a, scale_a_numel, scale_b,
+                             scale_b_numel, bias, m, n, k, lda, ldb, n, 0u, nullptr, 0,
+                             tmw::as_stream(stream), nullptr, nullptr, nullptr, &spec);
 }
 
 int tm_scaled_mm_i8_workspace_size(int64_t m, int64_t n, int64_t k, uint64_t* bytes) {

@@ -270,6 +270,53 @@ void scaled_mm_i8_lora(at::Tensor& out, const at::Tensor& a, const at::Tensor& b
                "scaled_mm_i8_lora");
 }
 
+// Merged QKV projection into the Ulysses all-to-all send buffer
+// send [world, 3, m, heads / world * head_dim] (tm_scaled_mm_i8_ulysses_send).
+void scaled_mm_i8_ulysses_send(at::Tensor& send, const at::Tensor& a, const at::Tensor& b,
+                               const at::Tensor& a_scales, const at::Tensor& b_scales,
+                               const std::optional<at::Tensor>& bias, int64_t num_heads,
+                               int64_t head_dim, int64_t world) {
+  check_cuda(a, a, "a");
+  check_cuda(b, a, "b");
+  check_cuda(send, a, "send");
+  check_cuda(a_scales, a, "a_scales");
+  check_cuda(b_scales, a, "b_scales");
+  TORCH_CHECK(a.scalar_type() == at::kChar && b.scalar_type() == at::kChar,
+              "a and b must be int8");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2, "a and b must be 2-D");
+  const int64_t m = a.size(0), k = a.size(1), n = b.size(1);
+  TORCH_CHECK(b.size(0) == k, "a and b inner dimensions differ");
+  TORCH_CHECK(world > 0 && num_heads % world == 0, "heads must divide by the Ulysses degree");
+  TORCH_CHECK(n == 3 * num_heads * head_dim, "b must have 3 x heads x head_dim columns");
+  TORCH_CHECK(send.is_contiguous() && send.numel() == m * n,
+              "send must be a contiguous [world, 3, m, heads / world * head_dim] buffer");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(0) == 1, "a row-major, b column-major (weight.t())");
+  const int out_dt = dtype_code(send);
+  TORCH_CHECK(out_dt == TM_DTYPE_BF16 || out_dt == TM_DTYPE_FP16, "send must be bf16 or fp16");
+  TORCH_CHECK(a_scales.scalar_type() == at::kFloat && b_scales.scalar_type() == at::kFloat &&
+                  a_scales.is_contiguous() && b_scales.is_contiguous(),
+              "scales must be contiguous float32");
+  const void* bias_ptr = nullptr;
+  if (bias.has_value()) {
+    check_cuda(*bias, a, "bias");
+    TORCH_CHECK(bias->scalar_type() == send.scalar_type() && bias->numel() == n &&
+                    bias->is_contiguous(),
+                "bias must be contiguous [n] in the output dtype");
+    bias_ptr = bias->data_ptr();
+  }
+  const int64_t lda = m > 1 ? a.stride(0) : k;
+  const int64_t ldb = n > 1 ? b.stride(1) : k;
+  const c10::cuda::CUDAGuard guard(a.device());
+  check_status(tm_scaled_mm_i8_ulysses_send(send.data_ptr(), out_dt, a.data_ptr<int8_t>(),
+                                            b.data_ptr<int8_t>(), a_scales.data_ptr<float>(),
+                                            a_scales.numel(), b_scales.data_ptr<float>(),
+                                            b_scales.numel(), bias_ptr, m, n, k, lda, ldb,
+                                            static_cast<int>(num_heads),
+                                            static_cast<int>(head_dim), static_cast<int>(world),
+                                            stream_of(a)),
+               "scaled_mm_i8_ulysses_send");
+}
+
 void quantize_weight_int8(at::Tensor& q, at::Tensor& scales, const at::Tensor& w) {
   check_cuda(w, w, "weight");
   check_cuda(q, w, "q");
@@ -384,6 +431,9 @@ TORCH_LIBRARY(taomate_w8a8, m) {
   m.def(
       "scaled_mm_i8_lora(Tensor(a!) out, Tensor a, Tensor b, Tensor a_scales, Tensor b_scales, "
       "Tensor? bias, Tensor lora_t, Tensor lora_b, int epilogue) -> ()");
+  m.def(
+      "scaled_mm_i8_ulysses_send(Tensor(a!) send, Tensor a, Tensor b, Tensor a_scales, "
+      "Tensor b_scales, Tensor? bias, int num_heads, int head_dim, int world) -> ()");
   m.def("quantize_weight_int8(Tensor(a!) q, Tensor(b!) scales, Tensor w) -> ()");
   m.def(
       "modulate_int8_quant(Tensor(a!) out, Tensor(b!) scales, Tensor(c!)? hidden_out, Tensor x, "
@@ -399,6 +449,7 @@ TORCH_LIBRARY_IMPL(taomate_w8a8, CUDA, m) {
   m.impl("cutlass_scaled_mm", &cutlass_scaled_mm);
   m.impl("scaled_mm_i8_ex", &scaled_mm_i8_ex);
   m.impl("scaled_mm_i8_lora", &scaled_mm_i8_lora);
+  m.impl("scaled_mm_i8_ulysses_send", &scaled_mm_i8_ulysses_send);
   m.impl("quantize_weight_int8", &quantize_weight_int8);
   m.impl("modulate_int8_quant", &modulate_int8_quant);
   m.impl("rms_norm_modulate_int8_quant", &rms_norm_modulate_int8_quant);

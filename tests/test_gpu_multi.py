@@ -123,8 +123,32 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
                 prev = (y, y.cpu().clone())
                 ar_errors.append((m, n, k, call, err, close, nccl_close, kept))
             peer.close()
+        # Ulysses exchange of a merged QKV projection: the fused send layout
+        # through NCCL's all-to-all equals the reference path (permute the
+        # ordinary output, then the same all-to-all)
+        from oracle.w8a8_oracle import merged_qkv_send_layout
+        from taomate_hd_b200.ulysses import merged_qkv_sequence_to_heads_w8a8
+
+        heads, hd, tokens, d = 8, 128, 256, 512
+        g = torch.Generator(device=device).manual_seed(50 + rank)
+        qx = torch.randint(-127, 128, (tokens, d), generator=g, device=device, dtype=torch.int8)
+        gw = torch.Generator(device=device).manual_seed(60)
+        wx = torch.randint(-127, 128, (3 * heads * hd, d), generator=gw, device=device,
+                           dtype=torch.int8)
+        sx = torch.rand(tokens, 1, generator=g, device=device) * 1e-2
+        swx = torch.rand(3 * heads * hd, generator=gw, device=device) * 1e-3
+        got = merged_qkv_sequence_to_heads_w8a8(qx, sx, wx, swx, None, num_heads=heads,
+                                               head_dim=hd, group=group, world=world)
+        plain = ops.scaled_mm(qx, wx.t(), sx, swx.reshape(1, -1), torch.bfloat16)
+        send = merged_qkv_send_layout(plain, heads, hd, world)
+        recv = torch.empty_like(send)
+        torch.distributed.all_to_all_single(recv, send, group=group)
+        ref = recv.movedim(0, 1).contiguous().view(3, tokens * world, heads // world, hd)
+        torch.cuda.synchronize()
+        ulysses_ok = all(torch.equal(a, b) for a, b in zip(got, ref.unbind(0)))
         code = ctypes_status(_native)
-        result.update(ok=True, errors=errors, ar_errors=ar_errors, device_status=code)
+        result.update(ok=True, errors=errors, ar_errors=ar_errors, device_status=code,
+                      ulysses_ok=ulysses_ok)
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
     except Exception:
@@ -164,6 +188,7 @@ def test_fused_reduce_scatter_two_ranks(tmp_path):
         for (m, n, k, call, err, close, nccl_close, tol) in res["errors"]:
             assert close, f"rank {r} {m}x{n}x{k} call {call}: max err {err}"
             assert nccl_close, f"rank {r} {m}x{n}x{k} call {call}: differs from the NCCL path"
+        assert res["ulysses_ok"], f"rank {r}: Ulysses exchange differs from the reference path"
         for (m, n, k, call, err, close, nccl_close, kept) in res["ar_errors"]:
             assert close, f"all-reduce rank {r} {m}x{n}x{k} call {call}: max err {err}"
             assert nccl_close, f"all-reduce rank {r} {m}x{n}x{k} call {call}: differs from NCCL"
