@@ -334,6 +334,57 @@ def skinny_sweep(world: int, device: torch.device, flush: torch.Tensor) -> list[
     return rows
 
 
+def ulysses_send(device: torch.device, flush: torch.Tensor) -> list[dict]:
+    """768p merged QKV projection per Ulysses rank (tokens / degree rows,
+    all heads), written in the all-to-all send layout.
+
+    ``fused_us``: the GEMM whose epilogue stores the send layout directly;
+    ``permute_us``: the reference order, the token-major GEMM output then
+    the permute copy into ``[degree, 3, tokens, heads / degree, head_dim]``
+    (ulysses.py:153-163 of the reference).  Layout only: the exchange itself
+    is NCCL's all-to-all in both cases and is not timed here.
+    """
+    from taomate_hd_b200 import ops
+    from taomate_hd_b200.ulysses import qkv_send_buffer
+
+    g = torch.Generator(device=device).manual_seed(78)
+    n = 3 * HEADS * HEAD_DIM
+    w = torch.randint(-127, 128, (n, D), generator=g, device=device, dtype=torch.int8)
+    sw = torch.rand(n, generator=g, device=device) * 1e-3 + 1e-5
+    bias = (torch.randn(n, generator=g, device=device) * 0.01).to(torch.bfloat16)
+    rows, reps = [], 10
+    for degree in (2, 8):
+        m = BLOCK_TOKENS // degree
+        a = torch.randint(-127, 128, (m, D), generator=g, device=device, dtype=torch.int8)
+        sa = torch.rand(m, 1, generator=g, device=device) * 1e-2 + 1e-4
+
+        def fused():
+            return qkv_send_buffer(a, sa, w, sw, bias, num_heads=HEADS, head_dim=HEAD_DIM,
+                                   world=degree)
+
+        def permuted():
+            y = ops.scaled_mm(a, w.t(), sa, sw.reshape(1, -1), torch.bfloat16, bias)
+            return y.view(m, 3, degree, HEADS // degree, HEAD_DIM).permute(2, 1, 0, 3, 4) \
+                    .contiguous()
+
+        result = {"degree": degree, "tokens": m, "n": n, "k": D}
+        for name, fn in (("fused_us", fused), ("permute_us", permuted)):
+            for _ in range(3):
+                fn()
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(reps)]
+            for e0, e1 in ev:
+                flush.zero_()
+                e0.record()
+                fn()
+                e1.record()
+            torch.cuda.synchronize()
+            result[name] = round(1e3 * sum(e0.elapsed_time(e1) for e0, e1 in ev) / reps, 2)
+        rows.append(result)
+        del a, sa
+    return rows
+
+
 def run_ours(args) -> int:
     world, rank, local = setup_distributed(args)
     if not torch.cuda.is_available():
@@ -478,13 +529,15 @@ def run_ours(args) -> int:
         lora_stack = lora_block_stack(ctx, device, g, world, flush)
         torch.cuda.empty_cache()
         sweep = skinny_sweep(world, device, flush)
+        ulysses = ulysses_send(device, flush) if world == 1 else None
         extras = {"ms_per_768p_block_linear_chain": block_ms,
                   "block_768p_tops": block_ops / (block_ms * 1e-3) / 1e12,
                   "block_768p_config": f"M={BLOCK_TOKENS}, d={D}, QKV N={3 * HEADS * HEAD_DIM}, "
                                        f"out-proj, fc1 N={FFN} (+GELU), fc2; all-reduce after "
                                        f"row-parallel linears; no LoRA / modulate fusion",
                   "lora_block_stack_768p": lora_stack,
-                  "skinny_sweep": sweep}
+                  "skinny_sweep": sweep,
+                  "ulysses_send_768p": ulysses}
 
     if rank == 0:
         peaks = load_peaks()

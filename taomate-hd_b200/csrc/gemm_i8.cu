@@ -90,6 +90,14 @@ struct GemmArgs {
   // `uses` x rows_per_owner x N, and reduce this rank's rows from its own
   // slots (local HBM reads): sum in rank order, add red_bias, store to red_out.
   int world, rank, rows_per_owner;
+  // Owner-interleaved tile order (scatter and all-reduce modes, m_owners =
+  // world, else 0): raster M-block v is M-block v / m_owners of owner
+  // v % m_owners, so every wave of concurrent tiles covers all owners and
+  // each rank's NVLink egress stays busy through the whole GEMM.  In plain
+  // raster order the ranks would all push to the same few owners at once
+  // (sharing their ingress), and each rank would alternate between local
+  // writes and pushes.
+  int m_owners, mb_per_owner;
   uint32_t uses;  // 1-based count of calls made with this buffer set
   const __nv_bfloat16* red_bias;
   __nv_bfloat16* red_out;
@@ -105,7 +113,8 @@ struct GemmArgs {
   __nv_bfloat16* peer_out[kMaxPeers];
 };
 
-__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb,
+                                            int m_owners, int mb_per_owner) {
   const int group_size = kGroupM * num_n;
   const int group = tile / group_size;
   const int first_m = group * kGroupM;
@@ -113,6 +122,10 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int&
   const int local = tile - group * group_size;
   mb = first_m + local % gm;
   nb = local / gm;
+  if (m_owners > 1) {  // num_m == m_owners x mb_per_owner
+    const int owner = mb % m_owners;
+    mb = owner * mb_per_owner + mb / m_owners;
+  }
 }
 
 __device__ __forceinline__ float gelu_tanh(float x) {
@@ -944,7 +957,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int kb0 = (unit - tile * g.splits) * g.kb_per_split;
         const int kb1 = min(kb0 + g.kb_per_split, g.kblocks);
         int mb, nb;
-        tile_coords(tile, g.num_m, g.num_n, mb, nb);
+        tile_coords(tile, g.num_m, g.num_n, mb, nb, g.m_owners, g.mb_per_owner);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&bar.empty[stage], phase ^ 1u, bar.abort_flag, g.status)) {
             ok = false;
@@ -1035,14 +1048,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     ColPrefetch pf{};
     if (g.tma_store && static_cast<int>(blockIdx.x) < units) {
       int mb0, nb0;
-      tile_coords(static_cast<int>(blockIdx.x), g.num_m, g.num_n, mb0, nb0);
+      tile_coords(static_cast<int>(blockIdx.x), g.num_m, g.num_n, mb0, nb0, g.m_owners, g.mb_per_owner);
       pf = col_prefetch<OutT>(g, nb0 * BN + epi_h * kHalf, kHalf,
                               static_cast<int64_t>(mb0) * kBM + epi_row, lane);
     }
     for (int unit = blockIdx.x; unit < units; unit += gridDim.x) {
       const int tile = unit / g.splits;
       int mb, nb;
-      tile_coords(tile, g.num_m, g.num_n, mb, nb);
+      tile_coords(tile, g.num_m, g.num_n, mb, nb, g.m_owners, g.mb_per_owner);
       float sa_tile = 0.f;
       if (g.tma_store) {
         col_cache_store(stage, pf, kHalf, lane);
@@ -1051,7 +1064,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int next = unit + static_cast<int>(gridDim.x);
         if (next < units) {
           int mb1, nb1;
-          tile_coords(next, g.num_m, g.num_n, mb1, nb1);
+          tile_coords(next, g.num_m, g.num_n, mb1, nb1, g.m_owners, g.mb_per_owner);
           pf = col_prefetch<OutT>(g, nb1 * BN + epi_h * kHalf, kHalf,
                                   static_cast<int64_t>(mb1) * kBM + epi_row, lane);
         }
@@ -1171,7 +1184,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int tile = pair; ok && tile < tiles; tile += pairs) {
         int mb, nb;
-        tile_coords(tile, g.num_m, g.num_n, mb, nb);
+        tile_coords(tile, g.num_m, g.num_n, mb, nb, g.m_owners, g.mb_per_owner);
         const int a_row = mb * 2 * kBM + static_cast<int>(rank) * kBM;
         const int b_row = nb * BN + static_cast<int>(rank) * kBNHalf;
         for (int kb = 0; kb < g.kblocks; ++kb) {
@@ -1270,13 +1283,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     ColPrefetch pf{};
     if (g.tma_store && pair < tiles) {
       int mb0, nb0;
-      tile_coords(pair, g.num_m, g.num_n, mb0, nb0);
+      tile_coords(pair, g.num_m, g.num_n, mb0, nb0, g.m_owners, g.mb_per_owner);
       pf = col_prefetch<OutT>(g, nb0 * BN + epi_h * kHalf, kHalf,
                               static_cast<int64_t>(mb0) * 2 * kBM + epi_row, lane);
     }
     for (int tile = pair; tile < tiles; tile += pairs) {
       int mb, nb;
-      tile_coords(tile, g.num_m, g.num_n, mb, nb);
+      tile_coords(tile, g.num_m, g.num_n, mb, nb, g.m_owners, g.mb_per_owner);
       float sa_tile = 0.f;
       if (g.tma_store) {
         col_cache_store(stage, pf, kHalf, lane);
@@ -1284,7 +1297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (tile + pairs < tiles) {
           int mb1, nb1;
-          tile_coords(tile + pairs, g.num_m, g.num_n, mb1, nb1);
+          tile_coords(tile + pairs, g.num_m, g.num_n, mb1, nb1, g.m_owners, g.mb_per_owner);
           pf = col_prefetch<OutT>(g, nb1 * BN + epi_h * kHalf, kHalf,
                                   static_cast<int64_t>(mb1) * 2 * kBM + epi_row, lane);
         }
@@ -1522,7 +1535,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t lora_full_leader = map_to_cta(smem_u32(lora_full), 0);
       for (int tile = pair; ok && tile < tiles; tile += pairs) {
         int mb, nb;
-        tile_coords(tile, g.num_m, g.num_n, mb, nb);
+        tile_coords(tile, g.num_m, g.num_n, mb, nb, g.m_owners, g.mb_per_owner);
         const int a_row = mb * 2 * kBM + static_cast<int>(rank) * kBM;
         const int b_row = nb * BN + static_cast<int>(rank) * kBNHalf;
         for (int kb = 0; kb < g.kblocks; ++kb) {
@@ -1671,19 +1684,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     ColPrefetch pf{};
     if (pair < tiles) {
       int mb0, nb0;
-      tile_coords(pair, g.num_m, g.num_n, mb0, nb0);
+      tile_coords(pair, g.num_m, g.num_n, mb0, nb0, g.m_owners, g.mb_per_owner);
       pf = col_prefetch<OutT>(g, nb0 * BN + h * kBNHalf, kBNHalf,
                               static_cast<int64_t>(mb0) * 2 * kBM + epi_row, lane);
     }
     for (int tile = pair; tile < tiles; tile += pairs) {
       int mb, nb;
-      tile_coords(tile, g.num_m, g.num_n, mb, nb);
+      tile_coords(tile, g.num_m, g.num_n, mb, nb, g.m_owners, g.mb_per_owner);
       col_cache_store(region, pf, kBNHalf, lane);
       const float sa_tile = pf.sa;
       __syncwarp();
       if (tile + pairs < tiles) {
         int mb1, nb1;
-        tile_coords(tile + pairs, g.num_m, g.num_n, mb1, nb1);
+        tile_coords(tile + pairs, g.num_m, g.num_n, mb1, nb1, g.m_owners, g.mb_per_owner);
         pf = col_prefetch<OutT>(g, nb1 * BN + h * kBNHalf, kBNHalf,
                                 static_cast<int64_t>(mb1) * 2 * kBM + epi_row, lane);
       }
@@ -1756,6 +1769,8 @@ int launch_single(const Operands& op, GemmArgs args, int sms, cudaStream_t strea
   using L = Smem<BN, STAGES>;
   args.num_m = (args.M + kBM - 1) / kBM;
   args.num_n = (args.N + BN - 1) / BN;
+  args.m_owners = args.world;
+  args.mb_per_owner = args.world > 0 ? args.rows_per_owner / kBM : 0;
   CUtensorMap ta, tb;
   if (!encode_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, op.a, args.K, args.M, op.lda, kBK, kBM,
                       CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -1790,6 +1805,8 @@ int launch_pair(const Operands& op, GemmArgs args, int max_pairs, cudaStream_t s
   using L = Smem<BN / 2, STAGES>;
   args.num_m = (args.M + 2 * kBM - 1) / (2 * kBM);
   args.num_n = (args.N + BN - 1) / BN;
+  args.m_owners = args.world;
+  args.mb_per_owner = args.world > 0 ? args.rows_per_owner / (2 * kBM) : 0;
   CUtensorMap ta, tb;
   if (!encode_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, op.a, args.K, args.M, op.lda, kBK, kBM,
                       CU_TENSOR_MAP_SWIZZLE_128B) ||
