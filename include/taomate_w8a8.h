@@ -202,9 +202,12 @@ int tm_scaled_mm_i8_lora(void* out, int out_dtype, const int8_t* a, const int8_t
  * permute copy, src/taomate_hd/distributed/ulysses.py:153-212): the GEMM of
  * tm_cutlass_scaled_mm with n = 3 x num_heads x head_dim, whose epilogue
  * stores row r, column (qkv, head, d) at send[w][qkv][r][(head % lh) *
- * head_dim + d], w = head / lh, lh = num_heads / world; `send` is a
+ * head_dim + d], w = head / lh, lh = ceil(num_heads / world); `send` is a
  * contiguous [world][3][m][lh x head_dim] buffer to pass to the all-to-all.
- * num_heads % world == 0, head_dim % 32 == 0, m % 32 == 0.
+ * When world does not divide num_heads the slots of the padded heads
+ * (w * lh + h >= num_heads) are set to zero, as the reference's zero-padded
+ * head shards (ulysses.py:188-193, ulysses_layout.py:9-42).
+ * head_dim % 32 == 0, m % 32 == 0.
  */
 int tm_scaled_mm_i8_ulysses_send(void* send, int out_dtype, const int8_t* a, const int8_t* b,
                                  const float* scale_a, int64_t scale_a_numel,

@@ -238,11 +238,18 @@ def lora_column(
 
 def merged_qkv_send_layout(value: torch.Tensor, num_heads: int, head_dim: int,
                            world: int) -> torch.Tensor:
-    """``_merged_qkv_send_layout`` (distributed/ulysses.py:153-163):
-    ``[tokens, 3 * heads * head_dim]`` -> ``[world, 3, tokens, heads / world, head_dim]``."""
+    """The send buffer of ``merged_qkv_sequence_to_heads`` (distributed/
+    ulysses.py:166-204, ``_merged_qkv_send_layout`` :153-163):
+    ``[tokens, 3 * heads * head_dim]`` -> ``[world, 3, tokens, local, head_dim]``,
+    local = ceil(heads / world); when ``world`` does not divide ``heads`` the
+    heads are first padded with zero heads (:188-193)."""
     tokens = value.shape[0]
-    local = num_heads // world
-    return (value.view(tokens, 3, num_heads, head_dim).view(tokens, 3, world, local, head_dim)
+    packed = value.reshape(tokens, 3, num_heads, head_dim)
+    padding = -num_heads % world
+    if padding:
+        packed = torch.nn.functional.pad(packed, (0, 0, 0, padding))
+    local = (num_heads + padding) // world
+    return (packed.reshape(tokens, 3, world, local, head_dim)
             .permute(2, 1, 0, 3, 4).contiguous())
 
 

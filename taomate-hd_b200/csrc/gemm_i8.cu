@@ -67,10 +67,10 @@ struct GemmArgs {
   int tma_store;
   // Ulysses send layout (ul_world > 0; merged QKV projection, n = 3 x heads
   // x head_dim): the output is the all-to-all send buffer
-  // [ul_world][3][M][heads / ul_world x head_dim] (the reference's
-  // _merged_qkv_send_layout, distributed/ulysses.py:153-163) instead of
-  // [M][N]; see ulysses_coords.
-  int ul_world, ul_heads, ul_head_dim;
+  // [ul_world][3][M][ul_local x head_dim], ul_local = ceil(heads / ul_world)
+  // (the reference's _merged_qkv_send_layout, distributed/ulysses.py:153-193,
+  // with its zero-padded head shards) instead of [M][N]; see ulysses_coords.
+  int ul_world, ul_heads, ul_head_dim, ul_local;
   // Split-K (one-CTA kernel): each tile's K range is cut into `splits`
   // slices of kb_per_split k-blocks; every (tile, slice) unit stores its exact
   // int32 partial in ws[slice][M][N] and bumps tile_counters[tile]; the unit
@@ -338,19 +338,19 @@ __device__ __forceinline__ uint4* stage64_slot(uint8_t* stage, int row, int chun
 
 // Ulysses send layout: output column `col` (a multiple of 32, never crossing
 // a head) of row `row` goes to the send buffer viewed as
-// [ul_world * 3 * M rows][heads / ul_world * head_dim columns]: row
-// (w * 3 + qkv) * M + row, column (head % local_heads) * head_dim + d, with
+// [ul_world * 3 * M rows][ul_local * head_dim columns]: row
+// (w * 3 + qkv) * M + row, column (head % ul_local) * head_dim + d, with
 // qkv = col / (heads * head_dim), head = that part / head_dim and
-// w = head / local_heads.
+// w = head / ul_local.  Padded head slots (w * ul_local + h >= heads) are
+// never written here; the host zeroes them before the launch.
 __device__ __forceinline__ void ulysses_coords(const GemmArgs& g, int col, int64_t row, int& x,
                                                int64_t& y) {
   const int width = g.ul_heads * g.ul_head_dim;
   const int qkv = col / width;
   const int within = col - qkv * width;
   const int head = within / g.ul_head_dim;
-  const int local_heads = g.ul_heads / g.ul_world;
-  const int w = head / local_heads;
-  x = within - w * local_heads * g.ul_head_dim;
+  const int w = head / g.ul_local;
+  x = within - w * g.ul_local * g.ul_head_dim;
   y = static_cast<int64_t>(w * 3 + qkv) * g.M + row;
 }
 
@@ -1754,7 +1754,7 @@ bool encode_out_map(CUtensorMap* map, GemmArgs& args) {
                                      ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   if (args.ul_world > 0) {  // send buffer as [world * 3 * M][local heads x head_dim]
-    const uint64_t cols = static_cast<uint64_t>(args.ul_heads / args.ul_world) * args.ul_head_dim;
+    const uint64_t cols = static_cast<uint64_t>(args.ul_local) * args.ul_head_dim;
     return encode_tmap_2d(map, dt, args.out, cols, static_cast<uint64_t>(3) * args.ul_world * args.M,
                           cols * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
   }
@@ -2079,7 +2079,7 @@ int scaled_mm_impl(void* out, int out_dtype, const int8_t* a, const int8_t* b, c
   if (k % 16 != 0 || n % 16 != 0) return TM_ERR_SHAPE;
   const bool swiglu = (epilogue & TM_EPI_SWIGLU) != 0;
   if (ul != nullptr) {
-    if (ul->world < 1 || ul->heads < 1 || ul->heads % ul->world != 0) return TM_ERR_SHAPE;
+    if (ul->world < 1 || ul->heads < 1) return TM_ERR_SHAPE;
     if (ul->head_dim % 32 != 0 || n != 3LL * ul->heads * ul->head_dim) return TM_ERR_SHAPE;
     if (m % 32 != 0) return TM_ERR_SHAPE;  // a 32-row store box never crosses a group
     if (3LL * ul->world * m > 0x7fffffffLL) return TM_ERR_TOO_LARGE;
@@ -2141,6 +2141,7 @@ int scaled_mm_impl(void* out, int out_dtype, const int8_t* a, const int8_t* b, c
     args.ul_world = ul->world;
     args.ul_heads = ul->heads;
     args.ul_head_dim = ul->head_dim;
+    args.ul_local = (ul->heads + ul->world - 1) / ul->world;
   }
   if (scatter != nullptr) {
     args.world = scatter->world;
@@ -2344,9 +2345,30 @@ int tm_scaled_mm_i8_ulysses_send(void* send, int out_dtype, const int8_t* a, con
                                  int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
                                  int num_heads, int head_dim, int world, void* stream) {
   const tmw::UlyssesSpec spec{num_heads, head_dim, world};
-  return tmw::scaled_mm_impl(send, out_dtype, a, b, scale_a, scale_a_numel, scale_b,
-                             scale_b_numel, bias, m, n, k, lda, ldb, n, 0u, nullptr, 0,
-                             tmw::as_stream(stream), nullptr, nullptr, nullptr, &spec);
+  const int rc = tmw::scaled_mm_impl(send, out_dtype, a, b, scale_a, scale_a_numel, scale_b,
+                                     scale_b_numel, bias, m, n, k, lda, ldb, n, 0u, nullptr, 0,
+                                     tmw::as_stream(stream), nullptr, nullptr, nullptr, &spec);
+  if (rc != TM_OK || m == 0) return rc;
+  // Zero-padded head shards (the reference pads num_heads up to a multiple of
+  // world with zero heads, distributed/ulysses.py:188-193): the padded slots
+  // h >= heads - w * local of each rank chunk w are never written by the
+  // GEMM; clear them, stream-ordered with it.
+  const int local = (num_heads + world - 1) / world;
+  const size_t row_bytes = static_cast<size_t>(local) * head_dim * 2;
+  for (int w = 0; w < world; ++w) {
+    const int real = num_heads - w * local;  // real heads in chunk w (may be <= 0)
+    const int first_pad = real < 0 ? 0 : (real > local ? local : real);
+    if (first_pad == local) continue;
+    for (int qkv = 0; qkv < 3; ++qkv) {
+      uint8_t* base = static_cast<uint8_t*>(send) +
+                      (static_cast<size_t>(w) * 3 + qkv) * static_cast<size_t>(m) * row_bytes +
+                      static_cast<size_t>(first_pad) * head_dim * 2;
+      if (cudaMemset2DAsync(base, row_bytes, 0, static_cast<size_t>(local - first_pad) * head_dim * 2,
+                            static_cast<size_t>(m), tmw::as_stream(stream)) != cudaSuccess)
+        return TM_ERR_CUDA;
+    }
+  }
+  return TM_OK;
 }
 
 int tm_scaled_mm_i8_workspace_size(int64_t m, int64_t n, int64_t k, uint64_t* bytes) {

@@ -271,7 +271,8 @@ void scaled_mm_i8_lora(at::Tensor& out, const at::Tensor& a, const at::Tensor& b
 }
 
 // Merged QKV projection into the Ulysses all-to-all send buffer
-// send [world, 3, m, heads / world * head_dim] (tm_scaled_mm_i8_ulysses_send).
+// send [world, 3, m, ceil(heads / world) * head_dim] (tm_scaled_mm_i8_ulysses_send;
+// padded head slots are zeroed).
 void scaled_mm_i8_ulysses_send(at::Tensor& send, const at::Tensor& a, const at::Tensor& b,
                                const at::Tensor& a_scales, const at::Tensor& b_scales,
                                const std::optional<at::Tensor>& bias, int64_t num_heads,
@@ -286,10 +287,11 @@ void scaled_mm_i8_ulysses_send(at::Tensor& send, const at::Tensor& a, const at::
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2, "a and b must be 2-D");
   const int64_t m = a.size(0), k = a.size(1), n = b.size(1);
   TORCH_CHECK(b.size(0) == k, "a and b inner dimensions differ");
-  TORCH_CHECK(world > 0 && num_heads % world == 0, "heads must divide by the Ulysses degree");
+  TORCH_CHECK(world > 0 && num_heads > 0, "heads and the Ulysses degree must be positive");
   TORCH_CHECK(n == 3 * num_heads * head_dim, "b must have 3 x heads x head_dim columns");
-  TORCH_CHECK(send.is_contiguous() && send.numel() == m * n,
-              "send must be a contiguous [world, 3, m, heads / world * head_dim] buffer");
+  const int64_t local = (num_heads + world - 1) / world;
+  TORCH_CHECK(send.is_contiguous() && send.numel() == world * 3 * m * local * head_dim,
+              "send must be a contiguous [world, 3, m, ceil(heads / world) * head_dim] buffer");
   TORCH_CHECK(a.stride(1) == 1 && b.stride(0) == 1, "a row-major, b column-major (weight.t())");
   const int out_dt = dtype_code(send);
   TORCH_CHECK(out_dt == TM_DTYPE_BF16 || out_dt == TM_DTYPE_FP16, "send must be bf16 or fp16");

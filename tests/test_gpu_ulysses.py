@@ -2,8 +2,9 @@
 
 Reference behaviour: ``merged_qkv_sequence_to_heads`` / ``_merged_qkv_send_layout``
 (src/taomate_hd/distributed/ulysses.py:153-212) permutes the merged QKV output
-``[tokens, 3 * heads * head_dim]`` into ``[world, 3, tokens, heads / world,
-head_dim]`` before the all-to-all.  The fused epilogue writes that buffer
+``[tokens, 3 * heads * head_dim]`` into ``[world, 3, tokens, ceil(heads /
+world), head_dim]`` before the all-to-all, padding with zero heads when the
+degree does not divide the heads (:188-193).  The fused epilogue writes that buffer
 directly: it must equal the reference permute of the ordinary GEMM output bit
 for bit (same epilogue arithmetic, different store coordinates).
 """
@@ -32,6 +33,9 @@ def _operands(tokens, d, n, seed, cuda):
     (256, 512, 8, 2, True),
     (320, 1024, 8, 4, False),     # tokens not a multiple of the 128-row tile
     (2048, 3072, 24, 8, True),    # 768p head layout at Ulysses 8
+    (320, 512, 6, 4, True),       # zero-padded head shards (local 2, 2 padded heads)
+    (256, 1024, 24, 5, False),    # one padded head in the last shard
+    (128, 256, 2, 4, False),      # fewer heads than ranks: whole shards of zeros
 ])
 def test_send_layout_matches_reference_permute(tm_ops, cuda, tokens, d, heads, world, with_bias):
     from taomate_hd_b200.ulysses import qkv_send_buffer
@@ -65,6 +69,9 @@ def test_send_layout_argument_errors(tm_ops, cuda):
     q, w, sq, sw, _ = _operands(100, 256, 3 * 4 * 128, seed=4, cuda=cuda)
     with pytest.raises(RuntimeError):  # 100 tokens: not a multiple of 32
         qkv_send_buffer(q, sq, w, sw, None, num_heads=4, head_dim=128, world=2)
-    q2, w2, sq2, sw2, _ = _operands(128, 256, 3 * 6 * 128, seed=5, cuda=cuda)
-    with pytest.raises(RuntimeError):  # 6 heads over 4 ranks
-        qkv_send_buffer(q2, sq2, w2, sw2, None, num_heads=6, head_dim=128, world=4)
+    q2, w2, sq2, sw2, _ = _operands(128, 256, 3 * 4 * 128, seed=5, cuda=cuda)
+    with pytest.raises(RuntimeError):  # head_dim 64 x 3 x 4 != the weight's 1536 rows
+        qkv_send_buffer(q2, sq2, w2, sw2, None, num_heads=4, head_dim=64, world=2)
+    from taomate_hd_b200.ulysses import merged_qkv_sequence_to_heads_w8a8
+    with pytest.raises(ValueError):  # the reference's width check
+        merged_qkv_sequence_to_heads_w8a8(q2, sq2, w2, sw2, None, num_heads=4, head_dim=64)

@@ -6,6 +6,9 @@
                           on sm_100, so vLLM's Triton implementation of the op)
 * ``reference_host.npz``  the reference's own torch code run on CPU
                           (tests/golden/make_reference_golden.py)
+* ``ulysses_send.npz``    the reference's ``merged_qkv_sequence_to_heads``
+                          send buffers and outputs, zero-head padding
+                          included (tests/golden/make_ulysses_golden.py)
 """
 from __future__ import annotations
 
@@ -136,3 +139,39 @@ def test_modulate_rounding_steps():
     xf, sf, shf = x.float(), scale.float(), shift.float()
     expect = ((xf * (1 + sf).to(torch.bfloat16).float()).to(torch.bfloat16).float() + shf).to(torch.bfloat16)
     assert torch.equal(h, expect)
+
+
+def _ulysses_cases():
+    data = np.load(GOLDEN / "ulysses_send.npz")
+    i = 0
+    while f"case{i}_shape" in data:
+        tokens, heads, head_dim, degree = (int(v) for v in data[f"case{i}_shape"])
+        send = _bf16(data[f"case{i}_send"]) if f"case{i}_send" in data else None
+        yield (tokens, heads, head_dim, degree, _bf16(data[f"case{i}_value"]),
+               _bf16(data[f"case{i}_qkv"]), send)
+        i += 1
+
+
+def test_oracle_ulysses_send_layout_matches_reference():
+    seen_padding = False
+    for tokens, heads, head_dim, degree, value, qkv, send in _ulysses_cases():
+        if send is None:
+            continue
+        got = orc.merged_qkv_send_layout(value, heads, head_dim, degree)
+        assert got.shape == send.shape
+        assert torch.equal(got.view(torch.int16), send.view(torch.int16))
+        seen_padding |= heads % degree != 0
+    assert seen_padding
+
+
+def test_ulysses_receive_layout_matches_reference():
+    """The reference's outputs were taken with an identity exchange, so its
+    (q, k, v) are the receive layout of its own send buffer."""
+    from taomate_hd_b200.ulysses import exchange_qkv, receive_layout
+
+    for tokens, heads, head_dim, degree, value, qkv, send in _ulysses_cases():
+        if send is None:  # degree 1: no exchange, q/k/v straight from the projection
+            got = exchange_qkv(orc.merged_qkv_send_layout(value, heads, head_dim, 1))
+        else:
+            got = receive_layout(send)
+        assert torch.equal(torch.stack(got).view(torch.int16), qkv.view(torch.int16))

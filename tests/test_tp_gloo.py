@@ -174,6 +174,46 @@ def test_tp_semantics_world2(tmp_path):
         assert 0 < res["row_close_to_full"] < 0.1
 
 
+def _ulysses_worker(rank: int, world: int, port: int, out_dir: str) -> None:
+    """Ulysses exchange of merged QKV send buffers (the oracle's layout, with
+    zero-head padding: 3 heads over 2 ranks) through exchange_qkv: rank r
+    must receive heads [r L, (r + 1) L) of every rank's tokens, in rank order
+    (distributed/ulysses.py:166-212)."""
+    result = {"rank": rank, "ok": False}
+    try:
+        _init(rank, world, port)
+        from oracle import w8a8_oracle as orc
+        from taomate_hd_b200.ulysses import exchange_qkv
+
+        tokens, heads, head_dim = 5, 3, 4
+        local = -(-heads // world)
+
+        def value_of(r):
+            g = torch.Generator().manual_seed(90 + r)
+            return torch.randn(tokens, 3 * heads * head_dim, generator=g).to(torch.bfloat16)
+
+        send = orc.merged_qkv_send_layout(value_of(rank), heads, head_dim, world)
+        got = exchange_qkv(send, group=torch.distributed.group.WORLD)
+        padded = [torch.nn.functional.pad(value_of(r).view(tokens, 3, heads, head_dim),
+                                          (0, 0, 0, world * local - heads)) for r in range(world)]
+        ok = True
+        for qkv in range(3):
+            want = torch.cat([p[:, qkv, rank * local:(rank + 1) * local] for p in padded])
+            ok &= got[qkv].shape == (tokens * world, local, head_dim)
+            ok &= torch.equal(got[qkv].view(torch.int16), want.view(torch.int16))
+        result.update(ok=True, exchange_exact=bool(ok))
+        torch.distributed.destroy_process_group()
+    except Exception:
+        result["error"] = traceback.format_exc()
+    Path(out_dir, f"rank{rank}.pkl").write_bytes(pickle.dumps(result))
+
+
+def test_ulysses_exchange_world2(tmp_path):
+    for res in _run(_ulysses_worker, 2, tmp_path):
+        assert res["ok"], res.get("error")
+        assert res["exchange_exact"]
+
+
 def _failure_worker(rank: int, world: int, port: int, out_dir: str) -> None:
     result = {"rank": rank}
     try:
