@@ -347,6 +347,26 @@ int tm_rms_norm_modulate_int8_quant(int8_t* out, float* scales, void* hidden_out
                                     int64_t table_stride, int64_t rows, int64_t cols,
                                     void* stream);
 
+/*
+ * Gated residual add + RMSNorm + adaLN modulate fused into the dynamic
+ * per-token quantisation: the producer of the fc1 input after attention.
+ * Follows _residual_gate_rms_norm_modulate_kernel
+ * (src/taomate_hd/inference/fused_kernels.py:349-382, wrapper :757-797):
+ *   t    = index ? index[r] : r
+ *   x    = bf16(residual[r,c] + bf16(gate[t,c] * branch[r,c]))  -> residual_out
+ *   n    = bf16(x * rsqrt(mean(x^2) + eps) * norm_weight)
+ *   h    = bf16(bf16(n * bf16(1 + scale[t,c])) + shift[t,c])   -> hidden_out
+ * then h is quantised as tm_dynamic_scaled_int8_quant.  All tensors bf16;
+ * gate, shift and scale rows share table_stride (the reference passes
+ * gate.stride(0) for all three).  residual_out is required, hidden_out may
+ * be NULL.
+ */
+int tm_residual_gate_rms_norm_modulate_int8_quant(
+    int8_t* out, float* scales, void* residual_out, void* hidden_out, const void* residual,
+    const void* branch, const void* gate, const void* norm_weight, float eps, const void* shift,
+    const void* scale, const int64_t* index, int64_t table_stride, int64_t rows, int64_t cols,
+    void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -21,8 +21,9 @@ computation of one step of the reference path:
 * weight quant      -> ``_quantize_cutlass_w8a8_weight`` (w8a8.py:175-179),
   pinned against the reference function itself by
   ``tests/golden/reference_host.npz`` (``tests/golden/make_reference_golden.py``).
-* adaLN producers   -> ``_modulate_kernel`` (fused_kernels.py:220-236) and
-  ``_rms_norm_modulate_kernel`` (fused_kernels.py:322-347).
+* adaLN producers   -> ``_modulate_kernel`` (fused_kernels.py:220-236),
+  ``_rms_norm_modulate_kernel`` (fused_kernels.py:322-347) and
+  ``_residual_gate_rms_norm_modulate_kernel`` (fused_kernels.py:349-382).
 * LoRA composition  -> ``H3InferenceParallelLinearLoRA.forward``
   (lora_checkpoint.py:126-154).
 * TP sharding       -> ``ColumnParallelLinear`` / ``MergedColumnParallelLinear`` /
@@ -223,6 +224,28 @@ def rms_norm_modulate(
     rinv = (1.0 / np.sqrt(var.astype(F32) + F32(eps))).astype(F32)
     n = round_bf16((xf * rinv[:, None]).astype(F32) * to_f32(weight)[None, :])
     return modulate(torch.from_numpy(n).to(torch.bfloat16).reshape(x.shape), shift, scale, index)
+
+
+def residual_gate_rms_norm_modulate(
+    residual: torch.Tensor,
+    branch: torch.Tensor,
+    gate: torch.Tensor,
+    weight: torch.Tensor,
+    eps: float,
+    shift: torch.Tensor,
+    scale: torch.Tensor,
+    index: torch.Tensor | None = None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """``_residual_gate_rms_norm_modulate_kernel`` (fused_kernels.py:349-382):
+    ``x = bf16(residual + bf16(gate[t] * branch))`` (returned as the new
+    residual), then :func:`rms_norm_modulate` of ``x``."""
+    rf = to_f32(residual).reshape(-1, residual.shape[-1])
+    bf = to_f32(branch).reshape(rf.shape)
+    rows = np.arange(rf.shape[0]) if index is None else index.cpu().numpy()
+    gt = to_f32(gate)[rows]
+    x = round_bf16(rf + round_bf16(gt * bf))
+    x_t = torch.from_numpy(x).to(torch.bfloat16).reshape(residual.shape)
+    return x_t, rms_norm_modulate(x_t, weight, eps, shift, scale, index)
 
 
 # ---------------------------------------------------------------- LoRA

@@ -81,6 +81,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tm_rms_norm_modulate_int8_quant": (
         c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p,
                 c_void_p, c_i64, c_i64, c_i64, c_void_p]),
+    "tm_residual_gate_rms_norm_modulate_int8_quant": (
+        c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                c_float, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_i64, c_void_p]),
 }
 
 

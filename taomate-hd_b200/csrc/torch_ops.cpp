@@ -419,6 +419,38 @@ void rms_norm_modulate_int8_quant(at::Tensor& out, at::Tensor& scales,
                "rms_norm_modulate_int8_quant");
 }
 
+void residual_gate_rms_norm_modulate_int8_quant(
+    at::Tensor& out, at::Tensor& scales, at::Tensor& residual_out,
+    const std::optional<at::Tensor>& hidden_out, const at::Tensor& residual,
+    const at::Tensor& branch, const at::Tensor& gate, const at::Tensor& weight, double eps,
+    const at::Tensor& shift, const at::Tensor& scale, const std::optional<at::Tensor>& index) {
+  const ModulateArgs r = check_modulate(out, scales, hidden_out, residual, shift, scale, index);
+  check_cuda(weight, residual, "weight");
+  check_cuda(branch, residual, "branch");
+  check_cuda(gate, residual, "gate");
+  check_cuda(residual_out, residual, "residual_out");
+  TORCH_CHECK(weight.scalar_type() == at::kBFloat16 && weight.is_contiguous() &&
+                  weight.numel() == r.cols,
+              "norm weight must be contiguous bfloat16 [cols]");
+  TORCH_CHECK(branch.scalar_type() == at::kBFloat16 && branch.is_contiguous() &&
+                  branch.sizes() == residual.sizes(),
+              "branch must be contiguous bfloat16 with the residual's shape");
+  TORCH_CHECK(residual_out.scalar_type() == at::kBFloat16 && residual_out.is_contiguous() &&
+                  residual_out.numel() == residual.numel(),
+              "residual_out must be contiguous bfloat16 with the residual's shape");
+  TORCH_CHECK(gate.scalar_type() == at::kBFloat16 && gate.sizes() == shift.sizes() &&
+                  gate.stride(1) == 1 && gate.stride(0) == shift.stride(0),
+              "gate must be a bfloat16 table shaped and strided like shift/scale");
+  const c10::cuda::CUDAGuard guard(residual.device());
+  check_status(tm_residual_gate_rms_norm_modulate_int8_quant(
+                   out.data_ptr<int8_t>(), scales.data_ptr<float>(), residual_out.data_ptr(),
+                   r.hidden, residual.data_ptr(), branch.data_ptr(), gate.data_ptr(),
+                   weight.data_ptr(), static_cast<float>(eps), shift.data_ptr(),
+                   scale.data_ptr(), r.index, r.table_stride, r.rows, r.cols,
+                   stream_of(residual)),
+               "residual_gate_rms_norm_modulate_int8_quant");
+}
+
 }  // namespace
 
 TORCH_LIBRARY(taomate_w8a8, m) {
@@ -443,6 +475,10 @@ TORCH_LIBRARY(taomate_w8a8, m) {
   m.def(
       "rms_norm_modulate_int8_quant(Tensor(a!) out, Tensor(b!) scales, Tensor(c!)? hidden_out, "
       "Tensor x, Tensor weight, float eps, Tensor shift, Tensor scale, Tensor? index) -> ()");
+  m.def(
+      "residual_gate_rms_norm_modulate_int8_quant(Tensor(a!) out, Tensor(b!) scales, "
+      "Tensor(c!) residual_out, Tensor(d!)? hidden_out, Tensor residual, Tensor branch, "
+      "Tensor gate, Tensor weight, float eps, Tensor shift, Tensor scale, Tensor? index) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(taomate_w8a8, CUDA, m) {
@@ -455,4 +491,6 @@ TORCH_LIBRARY_IMPL(taomate_w8a8, CUDA, m) {
   m.impl("quantize_weight_int8", &quantize_weight_int8);
   m.impl("modulate_int8_quant", &modulate_int8_quant);
   m.impl("rms_norm_modulate_int8_quant", &rms_norm_modulate_int8_quant);
+  m.impl("residual_gate_rms_norm_modulate_int8_quant",
+         &residual_gate_rms_norm_modulate_int8_quant);
 }

@@ -221,3 +221,30 @@ def rms_norm_modulate_int8_quant(
     hidden = torch.empty_like(x) if return_hidden else None
     _ops.rms_norm_modulate_int8_quant(q, s, hidden, x, weight, float(eps), shift, scale, index)
     return q, s, hidden
+
+
+def residual_gate_rms_norm_modulate_int8_quant(
+    residual: torch.Tensor,
+    branch: torch.Tensor,
+    gate: torch.Tensor,
+    weight: torch.Tensor,
+    eps: float,
+    shift: torch.Tensor,
+    scale: torch.Tensor,
+    index: torch.Tensor | None = None,
+    *,
+    return_hidden: bool = False,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor | None]:
+    """``fused_residual_gate_rms_norm_modulate`` (fused_kernels.py:349-382,
+    757-797) fused into the quant: returns the int8 rows and scales of the
+    modulated hidden state, the updated residual ``bf16(residual +
+    bf16(gate[t] * branch))`` and, if asked, the modulated hidden state."""
+    _require_cuda(residual, branch, gate, weight, shift, scale, index)
+    rows = residual.numel() // residual.shape[-1]
+    q = torch.empty_like(residual, dtype=torch.int8)
+    s = torch.empty((rows, 1), device=residual.device, dtype=torch.float32)
+    residual_out = torch.empty_like(residual)
+    hidden = torch.empty_like(residual) if return_hidden else None
+    _ops.residual_gate_rms_norm_modulate_int8_quant(
+        q, s, residual_out, hidden, residual, branch, gate, weight, float(eps), shift, scale, index)
+    return q, s, residual_out, hidden
