@@ -253,3 +253,41 @@ def test_stale_build_is_refused(monkeypatch):
 def test_backend_loader_returns_ops_module():
     backend = w8a8.require_vllm_cutlass_w8a8()
     assert callable(backend.scaled_int8_quant) and callable(backend.cutlass_scaled_mm)
+
+
+def _tile_coords(tile, num_m, num_n, m_owners, mb_per_owner, group_m=16):
+    """Restatement of the GEMM's tile_coords (grouped raster, then the
+    owner-interleaved M order of the fused reduce-scatter / all-reduce)."""
+    group_size = group_m * num_n
+    group = tile // group_size
+    first_m = group * group_m
+    gm = min(num_m - first_m, group_m)
+    local = tile - group * group_size
+    mb, nb = first_m + local % gm, local // gm
+    if m_owners > 1:
+        mb = (mb % m_owners) * mb_per_owner + mb // m_owners
+    return mb, nb
+
+
+@pytest.mark.parametrize("m,n,world,rows_per_mb,bn,ctas", [
+    (8192, 3072, 8, 256, 256, 74),    # fc2 at TP=8, CTA-pair tiles
+    (8192, 3072, 2, 256, 256, 74),
+    (20480, 3072, 8, 256, 256, 74),   # 768p out-proj at TP=8
+    (20480, 3072, 4, 128, 128, 148),  # one-CTA tiles
+    (2048, 1000, 2, 128, 64, 148),    # ragged N, one partial raster group
+])
+def test_interleaved_tile_order_is_a_permutation_covering_all_owners(m, n, world, rows_per_mb,
+                                                                     bn, ctas):
+    num_m, num_n = m // rows_per_mb, -(-n // bn)
+    mb_per_owner = (m // world) // rows_per_mb
+    assert num_m == world * mb_per_owner  # the host's m % (world x 256) check guarantees it
+    tiles = [_tile_coords(t, num_m, num_n, world, mb_per_owner) for t in range(num_m * num_n)]
+    assert sorted(tiles) == [(a, b) for a in range(num_m) for b in range(num_n)]
+    owner_of = [mb // mb_per_owner for mb, _ in tiles]
+    # every full wave of concurrent tiles sends to every owner, nearly evenly
+    for w0 in range(0, len(tiles) - ctas + 1, ctas):
+        counts = np.bincount(owner_of[w0:w0 + ctas], minlength=world)
+        assert counts.min() > 0 and counts.max() - counts.min() <= max(2, ctas // world // 2)
+    # without the interleave a wave covers only a few owners (what it fixes)
+    plain = [_tile_coords(t, num_m, num_n, 0, 0)[0] // mb_per_owner for t in range(ctas)]
+    assert len(set(plain)) <= -(-16 // mb_per_owner) + 1 < world or world <= 2
