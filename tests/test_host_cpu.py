@@ -291,3 +291,41 @@ def test_interleaved_tile_order_is_a_permutation_covering_all_owners(m, n, world
     # without the interleave a wave covers only a few owners (what it fixes)
     plain = [_tile_coords(t, num_m, num_n, 0, 0)[0] // mb_per_owner for t in range(ctas)]
     assert len(set(plain)) <= -(-16 // mb_per_owner) + 1 < world or world <= 2
+
+
+@pytest.mark.parametrize("world,rows,cols,match", [
+    (9, 8192, 3072, "1..8 ranks"),
+    (2, 8192 + 256, 3072, "multiple of 256"),
+    (8, 1024, 3072, "multiple of 256"),
+    (2, 8192, 3080, "multiple of 16"),
+])
+def test_peer_reduce_rejects_unsupported_shapes_before_allocating(world, rows, cols, match):
+    """Shape checks of the fused row-parallel reduction run on the host before
+    any allocation or collective, identically on every rank."""
+    from types import SimpleNamespace
+
+    from taomate_hd_b200.peer_reduce import PeerAllReduce, PeerReduceScatter
+
+    ctx = SimpleNamespace(tp_world_size=world, tp_rank=0, tp_group=None)
+    for cls in (PeerReduceScatter, PeerAllReduce):
+        with pytest.raises(ValueError, match=match):
+            cls(ctx, rows, cols, torch.device("cpu"))
+
+
+def test_ulysses_errors_match_reference_before_any_launch():
+    """merged_qkv_sequence_to_heads (distributed/ulysses.py:166-197): a weight
+    that is not 3 x heads x head_dim rows raises ValueError, and an exchange
+    without torch.distributed raises RuntimeError."""
+    from taomate_hd_b200.ulysses import exchange_qkv, merged_qkv_sequence_to_heads_w8a8
+
+    q = torch.zeros(64, 256, dtype=torch.int8)
+    s = torch.ones(64, 1)
+    w = torch.zeros(3 * 4 * 128, 256, dtype=torch.int8)
+    ws = torch.ones(3 * 4 * 128)
+    with pytest.raises(ValueError, match="merged QKV width"):
+        merged_qkv_sequence_to_heads_w8a8(q, s, w, ws, None, num_heads=4, head_dim=64)
+    assert not torch.distributed.is_initialized()
+    with pytest.raises(RuntimeError, match="initialized torch.distributed"):
+        merged_qkv_sequence_to_heads_w8a8(q, s, w, ws, None, num_heads=4, head_dim=128, world=2)
+    with pytest.raises(RuntimeError, match="initialized torch.distributed"):
+        exchange_qkv(torch.zeros(2, 3, 4, 2, 8, dtype=torch.bfloat16))
