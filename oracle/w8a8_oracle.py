@@ -23,7 +23,10 @@ computation of one step of the reference path:
   ``tests/golden/reference_host.npz`` (``tests/golden/make_reference_golden.py``).
 * adaLN producers   -> ``_modulate_kernel`` (fused_kernels.py:220-236),
   ``_rms_norm_modulate_kernel`` (fused_kernels.py:322-347) and
-  ``_residual_gate_rms_norm_modulate_kernel`` (fused_kernels.py:349-382).
+  ``_residual_gate_rms_norm_modulate_kernel`` (fused_kernels.py:349-382);
+  with ``swiglu`` (:298-309), pinned against those Triton kernels run by
+  Triton's CPU interpreter (``tests/golden/adaln_triton.npz``,
+  ``tests/golden/make_adaln_golden.py``).
 * LoRA composition  -> ``H3InferenceParallelLinearLoRA.forward``
   (lora_checkpoint.py:126-154).
 * TP sharding       -> ``ColumnParallelLinear`` / ``MergedColumnParallelLinear`` /

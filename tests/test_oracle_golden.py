@@ -6,6 +6,9 @@
                           on sm_100, so vLLM's Triton implementation of the op)
 * ``reference_host.npz``  the reference's own torch code run on CPU
                           (tests/golden/make_reference_golden.py)
+* ``adaln_triton.npz``    the reference's Triton adaLN producers and SwiGLU run
+                          by Triton's CPU interpreter
+                          (tests/golden/make_adaln_golden.py)
 * ``ulysses_send.npz``    the reference's ``merged_qkv_sequence_to_heads``
                           send buffers and outputs, zero-head padding
                           included (tests/golden/make_ulysses_golden.py)
@@ -175,3 +178,34 @@ def test_ulysses_receive_layout_matches_reference():
         else:
             got = receive_layout(send)
         assert torch.equal(torch.stack(got).view(torch.int16), qkv.view(torch.int16))
+
+
+def test_oracle_adaln_and_swiglu_match_reference_triton_kernels():
+    """fused_modulate / fused_gate_add / fused_rms_norm_modulate /
+    fused_residual_gate_rms_norm_modulate / fused_swiglu
+    (fused_kernels.py:643-797), executed by Triton's interpreter: the
+    oracle reproduces every output bit, including bf16 overflow to inf and
+    widths that leave a masked tail in the kernel's block."""
+    data = np.load(GOLDEN / "adaln_triton.npz")
+    for i in range(int(data["n_shapes"][0])):
+        g = lambda k: _bf16(data[f"s{i}_{k}"])
+        idx = torch.from_numpy(data[f"s{i}_indices"])
+        eps = float(data[f"s{i}_eps"][0])
+        x, branch, residual = g("x"), g("branch"), g("residual")
+        scale, shift, gate, weight = g("scale"), g("shift"), g("gate"), g("weight")
+
+        def same(got, name):
+            assert torch.equal(got.view(torch.int16), g(f"out_{name}").view(torch.int16)), name
+
+        with np.errstate(over="ignore", invalid="ignore"):
+            same(orc.modulate(x, shift, scale, idx), "modulate")
+            value, _ = orc.residual_gate_rms_norm_modulate(residual, branch, gate, weight, eps,
+                                                           shift, scale, idx)
+            same(value, "gate_add")
+            same(orc.rms_norm_modulate(x.clamp(-100, 100), weight, eps, shift, scale, idx),
+                 "rms_norm_modulate")
+            value, hidden = orc.residual_gate_rms_norm_modulate(
+                residual.clamp(-100, 100), branch, gate, weight, eps, shift, scale, idx)
+            same(value, "residual_gate_value")
+            same(hidden, "residual_gate_hidden")
+            same(orc.swiglu(g("swiglu_in")), "swiglu")
