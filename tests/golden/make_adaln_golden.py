@@ -14,8 +14,8 @@ therefore the kernels' own, while ``tl.rsqrt`` and ``tl.sum`` follow numpy
 (the GPU's approximate rsqrt and reduction tree may differ in the last bit),
 and ``tl.sigmoid`` is numpy's.
 
-Needs the reference tree (default ``/root/reference/src``, override with
-``TAOMATE_REFERENCE_SRC``); the output ``adaln_triton.npz`` is committed so
+Needs the reference tree (``TAOMATE_REFERENCE_SRC`` = its ``src``
+directory); the output ``adaln_triton.npz`` is committed so
 the tests never need the reference or Triton.
 
 Usage: ``python tests/golden/make_adaln_golden.py [outdir]``.
@@ -32,7 +32,10 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 HERE = Path(__file__).resolve().parent
-sys.path.insert(0, os.environ.get("TAOMATE_REFERENCE_SRC", "/root/reference/src"))
+_REFERENCE_SRC = os.environ.get("TAOMATE_REFERENCE_SRC")
+if not _REFERENCE_SRC:
+    raise SystemExit("set TAOMATE_REFERENCE_SRC to the reference checkout's src directory")
+sys.path.insert(0, _REFERENCE_SRC)
 
 # (rows, columns): a masked tail (200 of a 256-wide block) and a full block
 SHAPES = [(7, 200), (5, 256)]

@@ -1,8 +1,8 @@
 """Generate golden vectors by running the reference's own (pure-torch) code.
 
-Runs only where the reference tree is available (default
-``/root/reference/src``, override with ``TAOMATE_REFERENCE_SRC``); its output
-files are committed so the tests never need the reference at run time.
+Runs only where the reference tree is available (``TAOMATE_REFERENCE_SRC`` =
+its ``src`` directory); its output files are committed so the tests never
+need the reference at run time.
 
 Captured, each from the reference function named:
 
@@ -33,7 +33,10 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE.parent.parent))
-sys.path.insert(0, os.environ.get("TAOMATE_REFERENCE_SRC", "/root/reference/src"))
+_REFERENCE_SRC = os.environ.get("TAOMATE_REFERENCE_SRC")
+if not _REFERENCE_SRC:
+    raise SystemExit("set TAOMATE_REFERENCE_SRC to the reference checkout's src directory")
+sys.path.insert(0, _REFERENCE_SRC)
 
 from oracle import w8a8_oracle as orc  # noqa: E402
 

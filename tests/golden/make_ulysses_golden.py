@@ -5,8 +5,8 @@ ulysses.py:166-212) in a one-process ``gloo`` group with its ``_all_to_all``
 (:12-16) replaced by an identity copy, and records the send buffer the
 reference builds (``_merged_qkv_send_layout`` :153-163, with the zero-head
 padding of :188-193 when the degree does not divide the heads) and the
-(q, k, v) it returns from that buffer.  Needs the reference tree (default
-``/root/reference/src``, override with ``TAOMATE_REFERENCE_SRC``); the output
+(q, k, v) it returns from that buffer.  Needs the reference tree
+(``TAOMATE_REFERENCE_SRC`` = its ``src`` directory); the output
 ``ulysses_send.npz`` is committed so the tests never need the reference.
 
 Usage: ``python tests/golden/make_ulysses_golden.py [outdir]``.
@@ -23,7 +23,10 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-sys.path.insert(0, os.environ.get("TAOMATE_REFERENCE_SRC", "/root/reference/src"))
+_REFERENCE_SRC = os.environ.get("TAOMATE_REFERENCE_SRC")
+if not _REFERENCE_SRC:
+    raise SystemExit("set TAOMATE_REFERENCE_SRC to the reference checkout's src directory")
+sys.path.insert(0, _REFERENCE_SRC)
 
 # (tokens, heads, head_dim, degree): divisible, padded by 2, padded by 1, degree 1
 CASES = [(6, 4, 4, 2), (5, 6, 8, 4), (3, 24, 2, 5), (4, 3, 4, 1)]
