@@ -69,7 +69,8 @@ int tm_version(void);
  * Read (and optionally clear) the device status word of `device`: 0 when no
  * kernel of this library has recorded an error since the last clear,
  * otherwise a device status (1 = wait timeout, 2 = drain timeout).
- * Synchronises the device.
+ * Synchronises the device.  The word's address is looked up once per device
+ * and kept: do not use the library across a cudaDeviceReset.
  */
 int tm_device_status(int device, int* code, int clear);
 
@@ -228,10 +229,15 @@ int tm_scaled_mm_i8_ulysses_send(void* send, int out_dtype, const int8_t* a, con
  * Requests whose split needs more than that (a 64 KiB counter region plus
  * splits x m x n x 4 bytes) fail with TM_ERR_TOO_LARGE.  The first call on a
  * device looks up the array's device address (cudaGetSymbolAddress), so make
- * that first call before any stream capture.  Every call shares the one
- * array and clears its counters on `stream` before use: calls that overlap
- * on the GPU (other streams, other host threads) race and must be
- * serialised by the caller.  No counterpart in the reference.
+ * that first call before any stream capture.  The address is kept for the
+ * life of the process: the library must not be used across a
+ * cudaDeviceReset (or any other re-creation of the device's primary
+ * context).  Every call shares the one array and clears its counters on
+ * `stream` before use, after all argument checks have passed (a refused call
+ * enqueues nothing): calls that overlap on the GPU (other streams, other
+ * host threads) race and must be serialised by the caller.  TM_EPI_SWIGLU
+ * with splits > 1 returns TM_ERR_UNSUPPORTED.  Results are identical, bit
+ * for bit, to the unsplit GEMM.  No counterpart in the reference.
  */
 #define TM_SPLITK_NOALLOC_MAX_BYTES (16ull << 20)
 int tm_scaled_mm_i8_splitk_noalloc(void* out, int out_dtype, const int8_t* a, const int8_t* b,

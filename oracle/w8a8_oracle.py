@@ -219,8 +219,9 @@ def rms_norm_modulate(
     """RMSNorm then modulate (fused_kernels.py:322-347).
 
     ``n = bf16(x * rsqrt(mean(x^2) + eps) * w)`` with the mean accumulated in
-    float64 and the reciprocal square root rounded to fp32 (the device uses
-    a hardware rsqrt and another summation order: compare with a tolerance).
+    float64 and rounded to fp32, then ``1 / sqrt(var + eps)`` as two IEEE fp32
+    steps (square root, then reciprocal), as the reference's Triton kernel
+    evaluates it under the interpreter (pinned by ``adaln_triton.npz``).
     """
     xf = to_f32(x).reshape(-1, x.shape[-1])
     var = (xf.astype(np.float64) ** 2).mean(axis=1)

@@ -8,14 +8,21 @@ and adaLN pieces adjacent to the GEMM.
 
 Modules
 -------
-ops          vLLM-compatible ``scaled_int8_quant`` / ``cutlass_scaled_mm`` and fused variants
-w8a8         mirror of ``inference/w8a8.py`` (workspace, linear, weight conversion, policy)
-parallel     ``ParallelContext`` (``distributed/parallel.py``)
-collectives  NCCL reductions (``distributed/collectives.py``)
-linear       Column / MergedColumn / Row parallel linears (``distributed/linear.py``)
-lora         TP-aware LoRA wrapper (``inference/lora_checkpoint.py``)
-capi         ctypes binding of the C ABI (``include/taomate_w8a8.h``)
-build        in-tree build of the native libraries
+ops            vLLM-compatible ``scaled_int8_quant`` / ``cutlass_scaled_mm``, the
+               out-variant torch ops the reference's workspace calls, streamed
+               weight conversion and the fused variants
+fused_kernels  the reference's adaLN producer wrappers with the quant fused in
+peer_reduce    row-parallel GEMM with its reduce-scatter / all-reduce in the launch
+ulysses        merged QKV projection written in the Ulysses all-to-all send layout
+dit            TP-sharded DiT linear stages on preallocated buffers (bench workloads)
+parallel       ``ParallelContext`` (``distributed/parallel.py``)
+collectives    NCCL reductions (``distributed/collectives.py``)
+capi           ctypes binding of the C ABI (``include/taomate_w8a8.h``)
+build          in-tree build of the native libraries
+
+The reference's own host modules (``inference/w8a8.py``,
+``distributed/linear.py``, ``inference/lora_checkpoint.py``) run unchanged on
+top of ``ops``: they bind it by module name.
 """
 from __future__ import annotations
 

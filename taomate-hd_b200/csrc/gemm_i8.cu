@@ -676,6 +676,27 @@ __device__ __forceinline__ void reduce_block(const GemmArgs& g, int lrb, int col
   }
 }
 
+// After a bounded wait ran out, overwrite with NaN this CTA's share (the
+// tiles cta, cta + ctas, ... of a rows_per_owner x N block, the reduction's
+// own tiling) of an owner block that could not be produced, so that a
+// consumer reads NaN instead of stale or partial sums.  Local memory only:
+// nothing is written to a peer that may be gone.
+__device__ void poison_owner_block(const GemmArgs& g, __nv_bfloat16* block, int64_t ld, int bn,
+                                   int cta, int ctas) {
+  const int tiles = (g.rows_per_owner / kBM) * g.num_n;
+  const uint4 nan8 = make_uint4(0x7fc07fc0u, 0x7fc07fc0u, 0x7fc07fc0u, 0x7fc07fc0u);
+  for (int t = cta; t < tiles; t += ctas) {
+    const int lrb = t / g.num_n;
+    const int col0 = (t - lrb * g.num_n) * bn;
+    const int vec_per_row = min(bn, g.N - col0) / 8;
+    for (int v = threadIdx.x; v < kBM * vec_per_row; v += blockDim.x) {
+      const int r = v / vec_per_row;
+      const int c = col0 + (v - r * vec_per_row) * 8;
+      *reinterpret_cast<uint4*>(block + (static_cast<int64_t>(lrb) * kBM + r) * ld + c) = nan8;
+    }
+  }
+}
+
 // Fused reduce-scatter, owner side, run by every thread of a CTA that has no
 // GEMM tiles left (all CTAs of the cooperative persistent grid are resident,
 // and peers run concurrently on their own GPUs, so every wait here is on work
@@ -710,9 +731,15 @@ __device__ void reduce_phase(const GemmArgs& g, int bn, int cta, int ctas) {
       if (g.status) atomicExch(g.status, kDevWaitTimeout);
     }
   }
-  if (!__syncthreads_and(ok)) return;
+  const bool have_all = __syncthreads_and(ok) != 0;
   unsigned long long reduced = 0;
-  for (int t = cta; t < tiles; t += ctas) {
+  if (!have_all) {
+    // a source never reported: this rank's rows cannot be summed.  In
+    // all-reduce mode nothing is published either, so every rank's gather
+    // wait below runs out for this owner and poisons its copy of the rows.
+    poison_owner_block(g, g.red_out, g.red_ldo, bn, cta, ctas);
+  }
+  for (int t = cta; have_all && t < tiles; t += ctas) {
     const int lrb = t / g.num_n;
     const int nb = t - lrb * g.num_n;
     const int col0 = nb * bn;
@@ -729,7 +756,7 @@ __device__ void reduce_phase(const GemmArgs& g, int bn, int cta, int ctas) {
   // All-reduce: drain this CTA's gather stores once, publish the element
   // count to every rank, then wait until every owner's rows are here.
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (have_all && threadIdx.x == 0) {
     __threadfence_system();
     for (int j = 0; j < g.world; ++j)
       asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(g.peer_count[j] + g.world +
@@ -737,6 +764,9 @@ __device__ void reduce_phase(const GemmArgs& g, int bn, int cta, int ctas) {
                    "l"(reduced)
                    : "memory");
   }
+  __shared__ unsigned int missing;  // owners whose reduced rows never arrived
+  if (threadIdx.x == 0) missing = 0u;
+  __syncthreads();
   if (threadIdx.x < static_cast<unsigned>(g.world)) {
     const unsigned long long* c = g.peer_count[g.rank] + g.world + threadIdx.x;
     bool seen = ld_acquire_sys_u64(c) >= target;
@@ -747,8 +777,17 @@ __device__ void reduce_phase(const GemmArgs& g, int bn, int cta, int ctas) {
         __nanosleep(64);
       }
     }
-    if (!seen && g.status) atomicExch(g.status, kDevWaitTimeout);
+    if (!seen) {
+      if (g.status) atomicExch(g.status, kDevWaitTimeout);
+      atomicOr(&missing, 1u << threadIdx.x);
+    }
   }
+  __syncthreads();
+  const unsigned int lost = missing;
+  for (int j = 0; j < g.world; ++j)
+    if (lost & (1u << j))
+      poison_owner_block(g, g.peer_out[g.rank] + static_cast<int64_t>(j) * g.rows_per_owner * g.N,
+                         g.N, bn, cta, ctas);
   __syncthreads();
 }
 
@@ -1993,10 +2032,10 @@ struct SplitPlan {
   uint64_t bytes;
 };
 
-SplitPlan plan_split(int cfg, int splits, int m, int n, int kblocks) {
+SplitPlan plan_split(int cfg, int splits, int64_t m, int64_t n, int kblocks) {
   SplitPlan p{1, kblocks, 0, 0};
   if (splits <= 1 || cfg > kPairFlag) return p;
-  const int bn = cfg;
+  const int64_t bn = cfg;
   p.kb_per_split = (kblocks + splits - 1) / splits;
   p.splits = (kblocks + p.kb_per_split - 1) / p.kb_per_split;
   if (p.splits <= 1) {
@@ -2004,13 +2043,17 @@ SplitPlan plan_split(int cfg, int splits, int m, int n, int kblocks) {
     p.kb_per_split = kblocks;
     return p;
   }
-  const uint64_t tiles = static_cast<uint64_t>((m + kBM - 1) / kBM) * ((n + bn - 1) / bn);
+  // 64-bit tile arithmetic: m and n may be anything up to 2^31 - 1 here
+  const uint64_t tiles = static_cast<uint64_t>((m + kBM - 1) / kBM) *
+                         static_cast<uint64_t>((n + bn - 1) / bn);
   p.counter_bytes = kCounterRegion;
   if (tiles * 4 > kCounterRegion) {  // more tiles than counters: no workspace can hold it
     p.bytes = ~0ull;
     return p;
   }
-  p.bytes = p.counter_bytes + static_cast<uint64_t>(p.splits) * m * n * 4;
+  // tiles <= 16384 bounds m * n below 2^46, so the product cannot wrap
+  p.bytes = p.counter_bytes + static_cast<uint64_t>(p.splits) * static_cast<uint64_t>(m) *
+                                  static_cast<uint64_t>(n) * 4u;
   return p;
 }
 
@@ -2067,12 +2110,15 @@ struct Workspace {
   int force_splits;  // 0 = heuristic
 };
 
-int scaled_mm_impl(void* out, int out_dtype, const int8_t* a, const int8_t* b, const float* sa,
-                   int64_t sa_numel, const float* sb, int64_t sb_numel, const void* bias,
-                   int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldo,
-                   uint32_t epilogue, int32_t* acc_debug, int force_cfg, cudaStream_t stream,
-                   const ScatterSpec* scatter = nullptr, const Workspace* ws = nullptr,
-                   const LoraSpec* lora = nullptr, const UlyssesSpec* ul = nullptr) {
+// Host-side argument checks of every scaled-GEMM entry point: shapes,
+// strides, dtypes, epilogue flags, pointers and alignment.  Touches neither
+// the device nor the stream.  `ldo` may be adjusted (Ulysses layout).
+int validate_scaled_mm(const void* out, int out_dtype, const int8_t* a, const int8_t* b,
+                       const float* sa, int64_t sa_numel, const float* sb, int64_t sb_numel,
+                       const void* bias, int64_t m, int64_t n, int64_t k, int64_t lda,
+                       int64_t ldb, int64_t& ldo, uint32_t epilogue, const int32_t* acc_debug,
+                       const ScatterSpec* scatter, const LoraSpec* lora,
+                       const UlyssesSpec* ul) {
   if (out_dtype != TM_DTYPE_BF16 && out_dtype != TM_DTYPE_FP16) return TM_ERR_DTYPE;
   if (m < 0 || n <= 0 || k <= 0) return TM_ERR_SHAPE;
   if (m > 0x7fffffffLL || n > 0x7fffffffLL || k > 0x7fffffffLL) return TM_ERR_TOO_LARGE;
@@ -2118,6 +2164,19 @@ int scaled_mm_impl(void* out, int out_dtype, const int8_t* a, const int8_t* b, c
   if (!aligned16(a) || !aligned16(b) || !aligned16(out) || (bias && !aligned16(bias)) ||
       (sb_numel != 1 && !aligned16(sb)) || (acc_debug && !aligned16(acc_debug)))
     return TM_ERR_ALIGNMENT;
+  return TM_OK;
+}
+
+int scaled_mm_impl(void* out, int out_dtype, const int8_t* a, const int8_t* b, const float* sa,
+                   int64_t sa_numel, const float* sb, int64_t sb_numel, const void* bias,
+                   int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldo,
+                   uint32_t epilogue, int32_t* acc_debug, int force_cfg, cudaStream_t stream,
+                   const ScatterSpec* scatter = nullptr, const Workspace* ws = nullptr,
+                   const LoraSpec* lora = nullptr, const UlyssesSpec* ul = nullptr) {
+  const int rc = validate_scaled_mm(out, out_dtype, a, b, sa, sa_numel, sb, sb_numel, bias, m, n,
+                                    k, lda, ldb, ldo, epilogue, acc_debug, scatter, lora, ul);
+  if (rc != TM_OK || m == 0) return rc;
+  const bool swiglu = (epilogue & TM_EPI_SWIGLU) != 0;
   const int dev = current_device();
   const int sms = sm_count(dev);
   if (sms <= 0) return TM_ERR_CUDA;
@@ -2247,12 +2306,15 @@ int tm_scaled_mm_i8_splitk_noalloc(void* out, int out_dtype, const int8_t* a, co
                                    void* stream) {
   if (tile_n != 256 && tile_n != 128 && tile_n != 64) return TM_ERR_UNSUPPORTED;
   if (splits < 1 || splits > 64) return TM_ERR_UNSUPPORTED;
-  if (m < 0 || n <= 0 || k <= 0) return TM_ERR_SHAPE;
-  if (m > 0x7fffffffLL || n > 0x7fffffffLL || k > 0x7fffffffLL) return TM_ERR_TOO_LARGE;
-  if (m == 0) return TM_OK;
+  // every argument check runs before anything is enqueued on `stream`
+  int rc = tmw::validate_scaled_mm(out, out_dtype, a, b, scale_a, scale_a_numel, scale_b,
+                                   scale_b_numel, bias, m, n, k, lda, ldb, ldo, epilogue, nullptr,
+                                   nullptr, nullptr, nullptr);
+  if (rc != TM_OK || m == 0) return rc;
+  // the SwiGLU epilogue has no split-K form
+  if (splits > 1 && (epilogue & TM_EPI_SWIGLU)) return TM_ERR_UNSUPPORTED;
   const int kblocks = static_cast<int>((k + tmw::kBK - 1) / tmw::kBK);
-  const tmw::SplitPlan plan =
-      tmw::plan_split(tile_n, splits, static_cast<int>(m), static_cast<int>(n), kblocks);
+  const tmw::SplitPlan plan = tmw::plan_split(tile_n, splits, m, n, kblocks);
   // m * n fits 64 bits; bound it before trusting splits * m * n * 4
   const uint64_t mn = static_cast<uint64_t>(m) * static_cast<uint64_t>(n);
   if (plan.splits > 1 &&
@@ -2267,9 +2329,10 @@ int tm_scaled_mm_i8_splitk_noalloc(void* out, int out_dtype, const int8_t* a, co
       cudaMemsetAsync(scratch, 0, plan.counter_bytes, tmw::as_stream(stream)) != cudaSuccess)
     return TM_ERR_CUDA;
   const tmw::Workspace ws{scratch, tmw::kNoAllocScratchBytes, splits};
-  return tmw::scaled_mm_impl(out, out_dtype, a, b, scale_a, scale_a_numel, scale_b, scale_b_numel,
-                             bias, m, n, k, lda, ldb, ldo, epilogue, nullptr, tile_n,
-                             tmw::as_stream(stream), nullptr, &ws);
+  rc = tmw::scaled_mm_impl(out, out_dtype, a, b, scale_a, scale_a_numel, scale_b, scale_b_numel,
+                           bias, m, n, k, lda, ldb, ldo, epilogue, nullptr, tile_n,
+                           tmw::as_stream(stream), nullptr, &ws);
+  return rc;
 }
 
 
@@ -2384,7 +2447,7 @@ int tm_scaled_mm_i8_workspace_size(int64_t m, int64_t n, int64_t k, uint64_t* by
   const int max_pairs = tmw::max_resident_pairs(dev, sms);
   const tmw::Choice c = tmw::pick_choice(static_cast<int>(m), static_cast<int>(n), kblocks, sms,
                                          max_pairs, true);
-  *bytes = tmw::plan_split(c.cfg, c.splits, static_cast<int>(m), static_cast<int>(n), kblocks).bytes;
+  *bytes = tmw::plan_split(c.cfg, c.splits, m, n, kblocks).bytes;
   return TM_OK;
 }
 
@@ -2420,8 +2483,9 @@ int tm_scaled_mm_i8_splitk_workspace_size(int64_t m, int64_t n, int64_t k, int t
   if (bytes == nullptr) return TM_ERR_NULL_POINTER;
   if (tile_n != 256 && tile_n != 128 && tile_n != 64) return TM_ERR_UNSUPPORTED;
   if (m <= 0 || n <= 0 || k <= 0) return TM_ERR_SHAPE;
+  if (m > 0x7fffffffLL || n > 0x7fffffffLL || k > 0x7fffffffLL) return TM_ERR_TOO_LARGE;
   const int kblocks = static_cast<int>((k + tmw::kBK - 1) / tmw::kBK);
-  *bytes = tmw::plan_split(tile_n, splits, static_cast<int>(m), static_cast<int>(n), kblocks).bytes;
+  *bytes = tmw::plan_split(tile_n, splits, m, n, kblocks).bytes;
   return TM_OK;
 }
 

@@ -46,6 +46,7 @@ struct QuantParams {
   int64_t table_stride;
   const __nv_bfloat16* norm_w;
   float eps;
+  double inv_cols;  // 1 / cols, correctly rounded (RMSNorm modes)
   // kResGateRmsModulate: x is the residual stream; branch [rows, cols] and
   // the gate table (row stride table_stride) update it, and the updated
   // residual is written to residual_out [rows, cols]
@@ -165,6 +166,29 @@ __device__ __forceinline__ float group_reduce(float v, int tpr, float* red) {
   return v;
 }
 
+// Sum of one double per thread over the row group (the RMSNorm sum of
+// squares).  `red` must hold 8 doubles.
+__device__ __forceinline__ double group_sum_f64(double v, int tpr, double* red) {
+  const int lane_span = tpr < 32 ? tpr : 32;
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    if (off < lane_span) v = __dadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
+  }
+  if (tpr > 32) {
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    __syncthreads();  // protect `red` from the previous use
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    const int wpr = tpr >> 5;
+    const int first = (warp / wpr) * wpr;
+    double acc = red[first];
+    for (int w = 1; w < wpr; ++w) acc = __dadd_rn(acc, red[first + w]);
+    v = acc;
+  }
+  return v;
+}
+
 // Quantise a thread's VPT vectors of E values and store them.  kFast: the
 // FP32-pipe rounding (dynamic modes, rows where it equals the conversion);
 // chosen per row outside the loop so each path is straight-line code.
@@ -213,6 +237,68 @@ __device__ __forceinline__ float2 unpack_bf16x2(uint32_t w) {
   return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
 }
 
+// Correctly rounded fp32 square root and reciprocal without the library's
+// division / square-root subroutines (whose slow-path calls make the caller
+// save its live registers: the producers hold a whole row in registers).
+// Method: a hardware approximation (rsqrt.approx / rcp.approx, about 2^-22
+// relative), one Newton-Raphson step in fp64, rounding to fp32, then an exact
+// rounding test against the two neighbouring midpoints (Tuckerman's test):
+// a midpoint has at most 25 significant bits, so its square or its product
+// with a 24-bit value is exact in fp64 and the comparisons decide the
+// rounding exactly.  Exact midpoint ties cannot occur for either operation.
+__device__ __forceinline__ float f32_next_up(float v) {
+  return __uint_as_float(__float_as_uint(v) + 1u);  // v positive and finite
+}
+__device__ __forceinline__ float f32_next_down(float v) {
+  return __uint_as_float(__float_as_uint(v) - 1u);  // v positive
+}
+
+// fp32(sqrt(v)) for v positive, finite and normal.
+__device__ __forceinline__ float sqrt_rn_normal(float v) {
+  float y0;
+  asm("rsqrt.approx.f32 %0, %1;" : "=f"(y0) : "f"(v));
+  const double vd = static_cast<double>(v);
+  double y = static_cast<double>(y0);
+  // y <- y (3 - v y^2) / 2: Newton-Raphson for 1 / sqrt(v)
+  y = __dmul_rn(y, __fma_rn(-0.5 * vd, __dmul_rn(y, y), 1.5));
+  float s = __double2float_rn(__dmul_rn(vd, y));
+  const double hi = 0.5 * (static_cast<double>(s) + static_cast<double>(f32_next_up(s)));
+  const double lo = 0.5 * (static_cast<double>(s) + static_cast<double>(f32_next_down(s)));
+  if (vd >= __dmul_rn(hi, hi)) {
+    s = f32_next_up(s);
+  } else if (vd < __dmul_rn(lo, lo)) {
+    s = f32_next_down(s);
+  }
+  return s;
+}
+
+// fp32(1 / fp32(sqrt(v))), IEEE semantics for v >= 0 (and NaN).
+__device__ __forceinline__ float rsqrt_two_step_rn(float v) {
+  if (!(v > 0.0f)) return v == 0.0f ? __int_as_float(0x7f800000) : v;  // +inf / NaN
+  if (v == __int_as_float(0x7f800000)) return 0.0f;
+  float s;
+  if (v < 1.17549435e-38f) {  // subnormal: sqrt(v * 2^32) = sqrt(v) * 2^16, exactly
+    s = __fmul_rn(sqrt_rn_normal(__fmul_rn(v, 4294967296.0f)), 1.52587890625e-05f);
+  } else {
+    s = sqrt_rn_normal(v);
+  }
+  // s is normal here (s >= sqrt of the smallest subnormal), and so is 1 / s
+  float r0;
+  asm("rcp.approx.f32 %0, %1;" : "=f"(r0) : "f"(s));
+  const double sd = static_cast<double>(s);
+  double r = static_cast<double>(r0);
+  r = __fma_rn(r, __fma_rn(-sd, r, 1.0), r);  // r <- r (2 - s r)
+  float q = __double2float_rn(r);
+  const double hi = 0.5 * (static_cast<double>(q) + static_cast<double>(f32_next_up(q)));
+  const double lo = 0.5 * (static_cast<double>(q) + static_cast<double>(f32_next_down(q)));
+  if (__dmul_rn(sd, hi) <= 1.0) {  // 1 / s >= hi
+    q = f32_next_up(q);
+  } else if (__dmul_rn(sd, lo) > 1.0) {  // 1 / s < lo
+    q = f32_next_down(q);
+  }
+  return q;
+}
+
 // adaLN producers on a row held as packed bf16 (8 values per uint4; every
 // intermediate below is rounded to bf16, so the packed form loses nothing):
 //   kResGateRmsModulate: x = bf16(x + bf16(gate[t] * branch)) -> residual_out
@@ -224,7 +310,7 @@ __device__ __forceinline__ float2 unpack_bf16x2(uint32_t w) {
 template <int VPT, int MODE>
 __device__ __forceinline__ void adaln_rows(const QuantParams& p, uint4 (&raw)[VPT], int64_t row,
                                            int t, int tpr, int64_t nvec, bool active,
-                                           float* red) {
+                                           double* red) {
   constexpr int E = 8;
   const int64_t trow = active ? (p.index ? p.index[row] : row) : 0;
   if constexpr (MODE == kResGateRmsModulate) {
@@ -259,21 +345,38 @@ __device__ __forceinline__ void adaln_rows(const QuantParams& p, uint4 (&raw)[VP
   }
   float rinv = 0.f;
   if constexpr (MODE == kRmsModulate || MODE == kResGateRmsModulate) {
-    // variance = sum(x^2) / cols, summed in element order within a thread
-    float ss = 0.f;
+    // rinv = fp32(1 / fp32(sqrt(fp32(mean(x^2)) + eps))) with every step
+    // correctly rounded, as the reference kernel's arithmetic is restated by
+    // its oracle (a float64 mean, then IEEE fp32 add, sqrt and division; no
+    // approximate rsqrt).  The square of a bf16 value is exact in fp32; each
+    // thread sums its squares in four compensated fp32 chains (TwoSum: the
+    // rounding error of every add is kept in a second word), so s + c carries
+    // the sum to about 2^-40 relative; the pairs are then added in fp64.
+    float cs[4] = {0.f, 0.f, 0.f, 0.f}, cc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const uint32_t* xw = reinterpret_cast<const uint32_t*>(&raw[i]);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float2 x = unpack_bf16x2(xw[j]);
-        ss = __fadd_rn(ss, __fmul_rn(x.x, x.x));
-        ss = __fadd_rn(ss, __fmul_rn(x.y, x.y));
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float v = e ? x.y : x.x;
+          const float sq = __fmul_rn(v, v);
+          const float t = __fadd_rn(cs[j], sq);
+          const float z = __fsub_rn(t, cs[j]);
+          cc[j] = __fadd_rn(cc[j], __fadd_rn(__fsub_rn(cs[j], __fsub_rn(t, z)), __fsub_rn(sq, z)));
+          cs[j] = t;
+        }
       }
     }
-    ss = group_reduce<false>(ss, tpr, red);
-    const float variance = __fdiv_rn(ss, static_cast<float>(p.cols));
-    rinv = rsqrtf(__fadd_rn(variance, p.eps));
+    double ss = 0.0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      ss = __dadd_rn(ss, __dadd_rn(static_cast<double>(cs[j]), static_cast<double>(cc[j])));
+    ss = group_sum_f64(ss, tpr, red);
+    const float variance = __double2float_rn(__dmul_rn(ss, p.inv_cols));
+    rinv = rsqrt_two_step_rn(__fadd_rn(variance, p.eps));
   }
   const __nv_bfloat16* sc_row = p.mod_scale + trow * p.table_stride;
   const __nv_bfloat16* sh_row = p.shift + trow * p.table_stride;
@@ -319,7 +422,8 @@ template <typename T, int VPT, int MODE>
 __global__ void __launch_bounds__(256, (quant_min_blocks<MODE, VPT>())) quant_rows_kernel(
     const QuantParams p) {
   constexpr int E = VecTraits<T>::kElems;
-  __shared__ float red[8];
+  __shared__ double red_f64[8];  // the RMSNorm sum; also 8 floats for the maxima
+  float* red = reinterpret_cast<float*>(red_f64);
   const int tpr = 1 << p.tpr_log2;
   const int local_row = threadIdx.x >> p.tpr_log2;
   const int t = threadIdx.x & (tpr - 1);
@@ -345,7 +449,7 @@ __global__ void __launch_bounds__(256, (quant_min_blocks<MODE, VPT>())) quant_ro
       const int64_t vi = t + static_cast<int64_t>(i) * tpr;
       raw[i] = (active && vi < nvec) ? ld_stream16(xr + vi * E) : make_uint4(0u, 0u, 0u, 0u);
     }
-    if constexpr (kAdaLN) adaln_rows<VPT, MODE>(p, raw, row, t, tpr, nvec, active, red);
+    if constexpr (kAdaLN) adaln_rows<VPT, MODE>(p, raw, row, t, tpr, nvec, active, red_f64);
     __nv_bfloat162 m2 = __float2bfloat162_rn(0.0f), n2 = m2;
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
@@ -689,6 +793,7 @@ int tm_rms_norm_modulate_int8_quant(int8_t* out, float* scales, void* hidden_out
   p.table_stride = table_stride;
   p.norm_w = static_cast<const __nv_bfloat16*>(norm_weight);
   p.eps = eps;
+  p.inv_cols = 1.0 / static_cast<double>(cols);
   p.rows = rows;
   p.cols = cols;
   return tmw::launch_modulate<tmw::kRmsModulate>(p, tmw::as_stream(stream));
@@ -717,6 +822,7 @@ int tm_residual_gate_rms_norm_modulate_int8_quant(
   p.table_stride = table_stride;
   p.norm_w = static_cast<const __nv_bfloat16*>(norm_weight);
   p.eps = eps;
+  p.inv_cols = 1.0 / static_cast<double>(cols);
   p.branch = static_cast<const __nv_bfloat16*>(branch);
   p.gate = static_cast<const __nv_bfloat16*>(gate);
   p.residual_out = static_cast<__nv_bfloat16*>(residual_out);

@@ -52,30 +52,47 @@ def random_bf16(shape: tuple[int, ...], std: float, seed: int, device: torch.dev
     return (torch.randn(shape, generator=g, device=device, dtype=torch.float32) * std).to(torch.bfloat16)
 
 
+def column_slice(full: torch.Tensor, world: int, rank: int,
+                 output_sizes: tuple[int, ...] | None = None) -> torch.Tensor:
+    """This rank's output rows of a column-parallel weight, bias or LoRA B.
+
+    ``full`` stacks one or more logical projections along dim 0 (their row
+    counts in ``output_sizes``; one projection when None).  Every projection
+    is split into ``world`` equal parts on its own and the rank's parts are
+    stacked in projection order, so a merged QKV shard is ``[Q_r; K_r; V_r]``
+    and heads stay whole (the reference's per-projection merged sharding,
+    distributed/linear.py:207-215, lora_checkpoint.py:73-88).
+    """
+    sizes = output_sizes or (int(full.shape[0]),)
+    if sum(sizes) != full.shape[0]:
+        raise ValueError(f"output sizes {sizes} do not add up to {full.shape[0]} rows")
+    if any(s % world for s in sizes):
+        raise ValueError(f"every output size must divide by the TP degree {world}")
+    starts = torch.tensor([0, *sizes[:-1]]).cumsum(0).tolist()
+    parts = [full[start + rank * (s // world): start + (rank + 1) * (s // world)]
+             for start, s in zip(starts, sizes)]
+    return torch.cat(parts, 0).contiguous() if len(parts) > 1 else parts[0].contiguous()
+
+
+def row_slice(full: torch.Tensor, world: int, rank: int) -> torch.Tensor:
+    """This rank's input columns (the K slice) of a row-parallel weight or LoRA A
+    (distributed/linear.py:291-296, lora_checkpoint.py:91-97)."""
+    k = int(full.shape[-1])
+    if k % world:
+        raise ValueError(f"K ({k}) must divide by the TP degree {world}")
+    return full[..., rank * (k // world):(rank + 1) * (k // world)].contiguous()
+
+
 def column_weight(
     n: int, k: int, ctx: ParallelContext, seed: int, device: torch.device, *,
     bias: bool, output_sizes: tuple[int, ...] | None = None,
 ) -> W8Weight:
     """Column-parallel shard of a random [n, k] weight (per-projection for merged)."""
-    full = random_bf16((n, k), 0.02, seed, device)
     t, r = ctx.tp_world_size, ctx.tp_rank
-    sizes = output_sizes or (n,)
-    pieces, offset = [], 0
-    for size in sizes:
-        local = size // t
-        pieces.append(full.narrow(0, offset + r * local, local))
-        offset += size
-    local_w = torch.cat(pieces, 0).contiguous()
+    local_w = column_slice(random_bf16((n, k), 0.02, seed, device), t, r, output_sizes)
     q, s = ops.quantize_weight_int8(local_w)
-    b = None
-    if bias:
-        full_b = random_bf16((n,), 0.01, seed + 1, device)
-        pieces, offset = [], 0
-        for size in sizes:
-            local = size // t
-            pieces.append(full_b.narrow(0, offset + r * local, local))
-            offset += size
-        b = torch.cat(pieces, 0).contiguous()
+    b = (column_slice(random_bf16((n,), 0.01, seed + 1, device), t, r, output_sizes)
+         if bias else None)
     return W8Weight(q, s.reshape(-1), b)
 
 
@@ -83,9 +100,7 @@ def row_weight(
     n: int, k: int, ctx: ParallelContext, seed: int, device: torch.device, *, bias: bool
 ) -> W8Weight:
     """Row-parallel K-shard of a random [n, k] weight, quantised after sharding."""
-    full = random_bf16((n, k), 0.02, seed, device)
-    t, r = ctx.tp_world_size, ctx.tp_rank
-    local_w = full.narrow(1, r * (k // t), k // t).contiguous()
+    local_w = row_slice(random_bf16((n, k), 0.02, seed, device), ctx.tp_world_size, ctx.tp_rank)
     q, s = ops.quantize_weight_int8(local_w)
     b = random_bf16((n,), 0.01, seed + 1, device) if bias else None
     return W8Weight(q, s.reshape(-1), b)
@@ -273,22 +288,15 @@ def column_lora(n: int, k: int, rank: int, alpha: float, ctx: ParallelContext, s
     """Column LoRA shards (lora_checkpoint.py:73-88): full A, B sharded per projection."""
     a = random_bf16((rank, k), 0.02, seed, device)
     b_full = random_bf16((n, rank), 0.002, seed + 1, device)
-    t, r = ctx.tp_world_size, ctx.tp_rank
-    pieces, offset = [], 0
-    for size in output_sizes or (n,):
-        local = size // t
-        pieces.append(b_full.narrow(0, offset + r * local, local))
-        offset += size
-    b = (torch.cat(pieces, 0).float() * (alpha / rank)).to(torch.bfloat16).contiguous()
+    b_local = column_slice(b_full, ctx.tp_world_size, ctx.tp_rank, output_sizes)
+    b = (b_local.float() * (alpha / rank)).to(torch.bfloat16).contiguous()
     return LoRAShard(a, b)
 
 
 def row_lora(n: int, k: int, rank: int, alpha: float, ctx: ParallelContext, seed: int,
              device: torch.device) -> LoRAShard:
     """Row LoRA shards (lora_checkpoint.py:91-97): A sliced along K, full B."""
-    a_full = random_bf16((rank, k), 0.02, seed, device)
-    t, r = ctx.tp_world_size, ctx.tp_rank
-    a = a_full.narrow(1, r * (k // t), k // t).contiguous()
+    a = row_slice(random_bf16((rank, k), 0.02, seed, device), ctx.tp_world_size, ctx.tp_rank)
     b = (random_bf16((n, rank), 0.002, seed + 1, device).float() * (alpha / rank)).to(torch.bfloat16)
     return LoRAShard(a, b.contiguous())
 

@@ -181,6 +181,75 @@ def quantize_weight_int8(weight: torch.Tensor) -> tuple[torch.Tensor, torch.Tens
     return q, scales
 
 
+def quantize_weight_int8_into(
+    q_out: torch.Tensor,
+    scale_out: torch.Tensor,
+    source: torch.Tensor,
+    *,
+    staging_bytes: int = 8 << 20,
+) -> None:
+    """Convert a ``[N, K]`` weight into preallocated int8 storage, in row chunks.
+
+    For loaders that stream a checkpoint into already-allocated W8 slots (the
+    reference's ``load_cutlass_w8a8_stream_weight_``, w8a8.py:207-242): the
+    scales are per output row, so converting row chunks gives the same bytes
+    as converting the whole matrix.  ``q_out`` is int8 ``[N, K]`` and
+    ``scale_out`` fp32 with ``N`` elements, both contiguous on the GPU;
+    ``source`` is bf16/fp16/fp32 ``[N, K]`` on the host or the GPU.
+
+    A host source moves through two device staging buffers of at most
+    ``staging_bytes`` each: the copy of chunk i+1 runs on a side stream while
+    the kernel converts chunk i on the current stream, straight into the
+    output rows (no int8 temporary).  A contiguous source already on the
+    output's device is converted in one launch.  Stream-ordered; returns
+    without synchronising.
+    """
+    _require_cuda(q_out, scale_out)
+    if source.dtype not in (torch.bfloat16, torch.float16, torch.float32):
+        raise TypeError(f"source weight dtype {source.dtype} is not bf16, fp16 or fp32")
+    if q_out.dtype != torch.int8 or scale_out.dtype != torch.float32:
+        raise TypeError("q_out must be int8 and scale_out float32")
+    if source.dim() != 2 or tuple(q_out.shape) != tuple(source.shape):
+        raise ValueError(f"source {tuple(source.shape)} and q_out {tuple(q_out.shape)} "
+                         "must be the same 2-D shape")
+    if scale_out.numel() != source.shape[0]:
+        raise ValueError("scale_out needs one element per output row")
+    if not (q_out.is_contiguous() and scale_out.is_contiguous()):
+        raise ValueError("q_out and scale_out must be contiguous")
+    if staging_bytes <= 0:
+        raise ValueError("staging_bytes must be positive")
+    rows, cols = source.shape
+    if rows == 0:
+        return
+    scales = scale_out.view(-1)
+    device = q_out.device
+    if source.device == device and source.is_contiguous():
+        _ops.quantize_weight_int8(q_out, scales, source)
+        return
+    row_bytes = cols * source.element_size()
+    chunk = max(1, min(rows, staging_bytes // row_bytes))
+    staging = [torch.empty((chunk, cols), dtype=source.dtype, device=device) for _ in range(2)]
+    main = torch.cuda.current_stream(device)
+    side = torch.cuda.Stream(device)
+    copied = [torch.cuda.Event() for _ in range(2)]
+    consumed = [torch.cuda.Event() for _ in range(2)]
+    for i, start in enumerate(range(0, rows, chunk)):
+        stop = min(start + chunk, rows)
+        b = i % 2
+        dst = staging[b][: stop - start]
+        with torch.cuda.stream(side):
+            if i >= 2:
+                side.wait_event(consumed[b])
+            dst.copy_(source[start:stop], non_blocking=True)
+            copied[b].record(side)
+        main.wait_event(copied[b])
+        _ops.quantize_weight_int8(q_out[start:stop], scales[start:stop], dst)
+        consumed[b].record(main)
+    # The staging buffers belong to the current stream, and their last use
+    # is on it (every side-stream copy is waited on before its conversion),
+    # so freeing them here is stream-ordered after the last conversion.
+
+
 def modulate_int8_quant(
     x: torch.Tensor,
     shift: torch.Tensor,

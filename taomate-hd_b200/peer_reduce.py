@@ -20,6 +20,14 @@ for the all-reduce, a ``rows x cols`` output; shares it by CUDA IPC handle
 over the TP process group, and maps every peer's buffer once.  All ranks must
 call in the same order with the same shapes and tile configuration; the
 per-set use counts are kept identically on every rank.
+
+Failure reporting: every wait inside the kernel is bounded (1 s).  A wait
+that runs out (a peer that never contributes) records a device status word
+and overwrites the rows the kernel could not produce with NaN in this rank's
+own output; it never hangs.  The launch itself still returns success, because
+the host does not wait for the kernel: call :meth:`check` at a point where a
+device synchronisation is acceptable (or pass ``check_every=N`` to have every
+Nth call do it), which raises ``RuntimeError`` when the status word is set.
 """
 from __future__ import annotations
 
@@ -55,8 +63,12 @@ class _PeerBuffers:
 
     _gather = False
 
-    def __init__(self, ctx: ParallelContext, rows: int, cols: int, device: torch.device):
+    def __init__(self, ctx: ParallelContext, rows: int, cols: int, device: torch.device,
+                 *, check_every: int = 0):
         world, rank = ctx.tp_world_size, ctx.tp_rank
+        if check_every < 0:
+            raise ValueError("check_every must be >= 0")
+        self.check_every = check_every
         if world < 1 or world > 8:
             raise ValueError("the fused reduction supports 1..8 ranks")
         if rows % (256 * world):
@@ -124,6 +136,25 @@ class _PeerBuffers:
     def _raise(self, name: str, rc: int) -> None:
         raise RuntimeError(f"{name} failed: {self._lib.tm_status_string(rc).decode()}")
 
+    def _after_call(self) -> None:
+        if self.check_every and self.calls % self.check_every == 0:
+            self.check()
+
+    def check(self) -> None:
+        """Synchronise this rank's device and raise ``RuntimeError`` if a wait
+        inside one of this library's kernels ran out since the status word was
+        last cleared (a peer that never contributed: the rows it should have
+        produced hold NaN).  The word is left as it is."""
+        code = ctypes.c_int(0)
+        index = self.device.index if self.device.index is not None else torch.cuda.current_device()
+        rc = self._lib.tm_device_status(index, ctypes.byref(code), 0)
+        if rc != 0:
+            self._raise("tm_device_status", rc)
+        if code.value != 0:
+            raise RuntimeError(
+                f"fused row-parallel reduction on rank {self.rank}: a bounded device wait ran "
+                f"out (device status {code.value}); rows without all contributions hold NaN")
+
     def close(self) -> None:
         """Unmap the peers' buffers and free this rank's (after a device sync)."""
         if getattr(self, "_own", None) is None:
@@ -166,6 +197,7 @@ class PeerReduceScatter(_PeerBuffers):
             tile_n, stream)
         if rc != 0:
             self._raise("tm_scaled_mm_i8_reduce_scatter", rc)
+        self._after_call()
         return out
 
 
@@ -178,8 +210,9 @@ class PeerAllReduce(_PeerBuffers):
 
     _gather = True
 
-    def __init__(self, ctx: ParallelContext, rows: int, cols: int, device: torch.device):
-        super().__init__(ctx, rows, cols, device)
+    def __init__(self, ctx: ParallelContext, rows: int, cols: int, device: torch.device,
+                 *, check_every: int = 0):
+        super().__init__(ctx, rows, cols, device, check_every=check_every)
         # tensor views over this rank's own output of each set (the memory
         # belongs to this object and is freed by close())
         self._views = [_wrap_bf16(self._outs[h][self.rank], self.rows, self.cols, device)
@@ -198,4 +231,5 @@ class PeerAllReduce(_PeerBuffers):
             self._outs[half], self.world, self.rank, self._uses[half], tile_n, stream)
         if rc != 0:
             self._raise("tm_scaled_mm_i8_all_reduce", rc)
+        self._after_call()
         return self._views[half]

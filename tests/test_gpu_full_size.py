@@ -11,7 +11,10 @@ hold at any size:
   480p fc1 input (numpy handles 25 M elements in seconds);
 * the dequant epilogue is linear in the token scale: doubling ``scale_a``
   doubles every bf16 output exactly (a power-of-two factor commutes with
-  fp32 and bf16 rounding while nothing overflows).
+  fp32 and bf16 rounding while nothing overflows);
+* the bf16 outputs of the full-size linears (bias, GELU) are compared with
+  the oracle on a sample of rows: the oracle's exact int32 GEMM and fp32
+  epilogue handle a few hundred rows in seconds.
 """
 from __future__ import annotations
 
@@ -66,3 +69,28 @@ def test_full_size_epilogue_linear_in_token_scale(tm_ops, cuda, gelu):
     y2 = tm_ops.scaled_mm(a, b.t(), sa * 2, sb, torch.bfloat16, gelu_tanh=gelu)
     torch.cuda.synchronize()
     assert torch.equal(y2.float(), y1.float() * 2)
+
+
+@pytest.mark.parametrize("m,n,k,gelu", [
+    (8192, 12288, 3072, True),    # 480p fc1, bias + GELU-tanh
+    (8192, 3072, 12288, False),   # 480p fc2, bias
+    (20480, 9216, 3072, False),   # 768p merged QKV, bias
+])
+def test_full_size_bf16_outputs_match_oracle_on_sampled_rows(tm_ops, cuda, m, n, k, gelu):
+    x = orc.activation(m, k, seed=m + n)
+    w = orc.weight(n, k, seed=n + k)
+    g = torch.Generator().manual_seed(k)
+    bias = (torch.randn(n, generator=g) * 0.01).to(torch.bfloat16)
+    q, s, _ = tm_ops.scaled_int8_quant(x.to(cuda))
+    wq, ws = tm_ops.quantize_weight_int8(w.to(cuda))
+    y = tm_ops.scaled_mm(q, wq.t(), s, ws.t(), torch.bfloat16, bias.to(cuda), gelu_tanh=gelu)
+    torch.cuda.synchronize()
+    q_ref, s_ref = orc.dynamic_scaled_int8_quant(x)
+    wq_ref, ws_ref = orc.quantize_weight(w)
+    # rows on both sides of the first and last 128 / 256-row tile edges,
+    # plus a random sample
+    idx = np.unique(np.concatenate([
+        np.array([0, 1, 127, 128, 255, 256, m - 257, m - 256, m - 1]),
+        torch.randperm(m, generator=g)[:320].numpy()]))
+    ref, _ = orc.scaled_mm(q_ref[idx], wq_ref, s_ref[idx], ws_ref, bias, torch.bfloat16, gelu)
+    torch.testing.assert_close(y.cpu()[idx].float(), ref.float(), atol=1e-2, rtol=1e-2)

@@ -1,10 +1,12 @@
 """GPU: the allocation-free split-K entry point against the ordinary GEMM entry.
 
 ``tm_scaled_mm_i8_splitk_noalloc`` keeps its int32 partials and tile counters
-in a fixed array inside the library instead of a caller workspace.  Its
-outputs must agree with ``tm_scaled_mm_i8_ex`` (no split, no scratch) on the
-same operands, on consecutive calls that reuse the array, and requests whose
-split needs more than the array holds must be refused before any launch.
+in a fixed array inside the library instead of a caller workspace, for callers
+that must not allocate device memory.  The split sums exact int32 partials and
+runs the same epilogue, so its outputs must equal ``tm_scaled_mm_i8_ex`` (no
+split, no scratch) bit for bit on the same operands, on consecutive calls that
+reuse the array; requests whose split needs more than the array holds, and bad
+arguments, must be refused before anything is enqueued.
 The file name keeps it last in collection, so it also runs after every other
 GPU test has used the library in the same process.
 """
@@ -17,8 +19,8 @@ import torch
 
 pytestmark = pytest.mark.gpu
 
-ATOL = 1e-2
-RTOL = 1e-2
+TM_ERR_SHAPE = 2
+TM_ERR_ALIGNMENT = 3
 TM_ERR_UNSUPPORTED = 5
 TM_ERR_TOO_LARGE = 8
 
@@ -64,8 +66,7 @@ def test_no_alloc_matches_ordinary_entry_two_calls(capi, cuda, m, n, k, tile_n, 
                                                  tile_n, splits, _stream())
         assert rc == 0, capi.tm_status_string(rc)
         torch.cuda.synchronize()
-        torch.testing.assert_close(got.float().cpu(), ref.float().cpu(), atol=ATOL, rtol=RTOL,
-                                   msg=f"call {call}")
+        assert torch.equal(got, ref), f"call {call}: split-K output differs from the unsplit GEMM"
 
 
 def test_no_alloc_refuses_oversized_and_bad_arguments(capi, cuda):
@@ -83,3 +84,26 @@ def test_no_alloc_refuses_oversized_and_bad_arguments(capi, cuda):
     assert capi.tm_scaled_mm_i8_splitk_noalloc(*base, 0, 96, 2, _stream()) == TM_ERR_UNSUPPORTED
     assert capi.tm_scaled_mm_i8_splitk_noalloc(*base, 0, 64, 0, _stream()) == TM_ERR_UNSUPPORTED
     torch.cuda.synchronize()
+
+
+def test_no_alloc_checks_arguments_before_enqueueing(capi, cuda):
+    """Refused calls return their error before the counters are cleared on
+    the stream: an output left as NaN stays NaN, and the next valid call on
+    the same stream is exact."""
+    a, b, sa, sb, _ = _operands(64, 768, 12288, seed=3, cuda=cuda, with_bias=False)
+    got = torch.full((64, 768), float("nan"), dtype=torch.bfloat16, device=cuda)
+    args = list(_gemm_args(got, a, b, sa, sb, None))
+    bad_ld = args.copy()
+    bad_ld[12] = 12280  # lda < k
+    assert capi.tm_scaled_mm_i8_splitk_noalloc(*bad_ld, 0, 64, 4, _stream()) == TM_ERR_SHAPE
+    bad_align = args.copy()
+    bad_align[2] = a.data_ptr() + 8
+    assert capi.tm_scaled_mm_i8_splitk_noalloc(*bad_align, 0, 64, 4, _stream()) == TM_ERR_ALIGNMENT
+    assert capi.tm_scaled_mm_i8_splitk_noalloc(*args, 2, 64, 4, _stream()) == TM_ERR_UNSUPPORTED
+    torch.cuda.synchronize()
+    assert torch.isnan(got.float()).all()
+    ref = torch.empty_like(got)
+    assert capi.tm_scaled_mm_i8_ex(*_gemm_args(ref, a, b, sa, sb, None), 0, None, _stream()) == 0
+    assert capi.tm_scaled_mm_i8_splitk_noalloc(*args, 0, 64, 4, _stream()) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(got, ref)
