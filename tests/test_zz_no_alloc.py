@@ -74,11 +74,14 @@ def test_no_alloc_refuses_oversized_and_bad_arguments(capi, cuda):
     out = torch.empty(256, 128, dtype=torch.bfloat16, device=cuda)
     base = list(_gemm_args(out, a, b, sa, sb, None))
     # 2 slices x 256 x 12288 x 4 bytes = 24 MiB of partials: above the array
+    # (per-tensor scales keep the oversized requests valid in every other way)
     big = base.copy()
+    big[5], big[7] = 1, 1
     big[9:15] = [256, 12288, 12288, 12288, 12288, 12288]
     assert capi.tm_scaled_mm_i8_splitk_noalloc(*big, 0, 64, 2, _stream()) == TM_ERR_TOO_LARGE
     # sizes whose m * n * splits * 4 leaves 64 bits are refused, not wrapped
     huge = base.copy()
+    huge[5], huge[7] = 1, 1
     huge[9:15] = [1 << 30, 1 << 30, 1 << 20, 1 << 20, 1 << 20, 1 << 30]
     assert capi.tm_scaled_mm_i8_splitk_noalloc(*huge, 0, 64, 64, _stream()) == TM_ERR_TOO_LARGE
     assert capi.tm_scaled_mm_i8_splitk_noalloc(*base, 0, 96, 2, _stream()) == TM_ERR_UNSUPPORTED
