@@ -206,14 +206,56 @@ def time_cpu_reference(rows: int, min_seconds: float, max_passes: int) -> dict:
                       "(oracle quant + torch._int_mm + fp32 epilogue), TOPS of the sample"}
 
 
+def time_cpu_bf16_linear(rows: int, min_seconds: float, max_passes: int) -> dict:
+    """The repo-side BF16 baseline: ``nn.Linear`` (``F.linear``) for fc1 (+bias,
+    GELU-tanh) and fc2 (+bias) of ``rows`` tokens on the host cores."""
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(rows, D, generator=g).to(torch.bfloat16)
+    w1 = (torch.randn(FFN, D, generator=g) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn(D, FFN, generator=g) * 0.02).to(torch.bfloat16)
+    b1 = (torch.randn(FFN, generator=g) * 0.01).to(torch.bfloat16)
+    b2 = (torch.randn(D, generator=g) * 0.01).to(torch.bfloat16)
+    F = torch.nn.functional
+
+    def step():
+        return F.linear(F.gelu(F.linear(x, w1, b1), approximate="tanh"), w2, b2)
+
+    step()
+    times = []
+    t_end = time.perf_counter() + min_seconds
+    while len(times) < max_passes and (not times or time.perf_counter() < t_end):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    per = statistics.mean(times)
+    flops = 2 * 2 * rows * D * FFN
+    return {"value": flops / per / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+            "kind": "bf16 nn.Linear",
+            "sample": f"{rows} of {TOKENS} tokens, {len(times)} passes of {per * 1e3:.1f} ms "
+                      "(F.linear fc1 + GELU-tanh + F.linear fc2 in bf16)"}
+
+
 def run_reference(args) -> int:
+    """The reference's arithmetic for the path on the host cores, on the same
+    workload as our arm: every step quantises all 8192 tokens and runs fc1
+    (+bias, GELU) and fc2 (+bias) through the exact int32 GEMM and the fp32
+    epilogue.  Should K + W full steps not fit in about four minutes, each
+    step takes an equal token sample instead (``config.sample_tokens``)."""
     world, rank, _ = setup_distributed(args)
     if rank != 0:
         return 0
     torch.set_num_threads(os.cpu_count() or 1)
-    rows = 128
+    rows = TOKENS
     x, fc1, fc2 = cpu_reference_setup(rows)
-    for _ in range(args.warmup):
+    t0 = time.perf_counter()
+    cpu_reference_step(x, fc1, fc2)
+    first = time.perf_counter() - t0
+    budget_s = 240.0
+    if first * (args.steps + args.warmup) > budget_s:
+        rows = max(128, int(TOKENS * budget_s / (first * (args.steps + args.warmup))) // 128 * 128)
+        x, fc1, fc2 = cpu_reference_setup(rows)
+    for _ in range(args.warmup - 1):
         cpu_reference_step(x, fc1, fc2)
     t0 = time.perf_counter()
     for _ in range(args.steps):
@@ -221,19 +263,23 @@ def run_reference(args) -> int:
     per = (time.perf_counter() - t0) / args.steps
     ops = 2 * 2 * rows * D * FFN
     value = ops / per / 1e12
+    sample = (f"all {TOKENS} tokens per step" if rows == TOKENS else
+              f"{rows} of {TOKENS} tokens per step (time bound)")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": per * 1e3,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
         "data": "synthetic",
         "config": {"workload": WORKLOAD, "tokens": TOKENS, "d": D, "ffn": FFN,
-                   "parallelism": f"tp{args.gpus}", "sample_tokens": rows},
+                   "parallelism": "tp1 (host cores)", "sample_tokens": rows,
+                   "same_config": rows == TOKENS},
         "cpu_baseline": {"value": value, "unit": "TOPS", "cores": torch.get_num_threads(),
                          "kind": "port",
-                         "sample": f"{rows} of {TOKENS} tokens per step at TP=1 on the host cores "
-                                   "(the reference's arithmetic restated in oracle/; the reference's "
-                                   "own int8 GEMM (vLLM cutlass_scaled_mm) has no CPU path and "
-                                   "refuses int8 on sm_100)"},
+                         "sample": f"{sample} at TP=1 on the host cores (the reference's "
+                                   "arithmetic restated in oracle/: per-token quant, exact int32 "
+                                   "GEMM, fp32 epilogue; the reference's own int8 GEMM, vLLM "
+                                   "cutlass_scaled_mm, has no CPU path and refuses int8 on "
+                                   "sm_100)"},
         "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -291,12 +337,20 @@ def skinny_sweep(world: int, device: torch.device, flush: torch.Tensor) -> list[
     """the scaled GEMM over M at two weight shapes.
 
     Each rank runs the column-parallel shard (N / TP) of its own weight; no
-    collective.  Every launch is timed alone with CUDA events.  Before each,
-    L2 is flushed by writing 256 MiB and then reading another 256 MiB, so the
-    weights come from HBM and no dirty flush lines are left for the timed
-    kernel to write back (at small M that write-back would dominate).
-    ``hbm_gbs`` counts the minimum bytes MK + NK + 2MN + 4M + 4N once per
-    launch.
+    collective.  Every shape is launched before any is timed.  Two
+    measurements per shape:
+
+    * ``us``: each launch timed alone with CUDA events (median of 10).
+      Before each, L2 is flushed by writing 256 MiB and then reading another
+      256 MiB, so the weights come from HBM and no dirty flush lines are left
+      for the timed kernel to write back (at small M that would dominate).
+    * ``stream_us``: 64 launches back to back on one stream, each on its own
+      copy of the weight (the copies together exceed twice the L2), timed as
+      one region and divided by the launch count: the per-layer time of a
+      chain of linears, where one launch's set-up overlaps the previous one.
+
+    ``hbm_gbs`` / ``stream_hbm_gbs`` count the minimum bytes MK + NK + 2MN +
+    4M + 4N once per launch.
     """
     from taomate_hd_b200 import ops
 
@@ -304,33 +358,50 @@ def skinny_sweep(world: int, device: torch.device, flush: torch.Tensor) -> list[
     clean = torch.ones(FLUSH_BYTES // 4, dtype=torch.float32, device=device)
     sink = torch.empty((), dtype=torch.float32, device=device)
     rows = []
-    reps = 10
+    reps, chain = 10, 64
     for n_full, k in SWEEP_NK:
         n = n_full // world
-        w = torch.randint(-127, 128, (n, k), generator=g, device=device, dtype=torch.int8)
+        copies = max(2, -(-(2 * 126 * 2 ** 20) // (n * k)))  # > 2 x L2 of weights
+        ws = [torch.randint(-127, 128, (n, k), generator=g, device=device, dtype=torch.int8)
+              for _ in range(copies)]
         sb = torch.rand(1, n, generator=g, device=device) * 1e-3 + 1e-5
+        inputs = {}
         for m in SWEEP_M:
             a = torch.randint(-127, 128, (m, k), generator=g, device=device, dtype=torch.int8)
             sa = torch.rand(m, 1, generator=g, device=device) * 1e-2 + 1e-4
+            inputs[m] = (a, sa, torch.empty(m, n, dtype=torch.bfloat16, device=device))
             for _ in range(3):
-                ops.scaled_mm(a, w.t(), sa, sb, torch.bfloat16)
+                ops.scaled_mm(a, ws[0].t(), sa, sb, torch.bfloat16, out=inputs[m][2])
+        torch.cuda.synchronize()
+        for m in SWEEP_M:
+            a, sa, y = inputs[m]
             ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                   for _ in range(reps)]
             for e0, e1 in ev:
                 flush.zero_()
                 torch.sum(clean, dim=0, out=sink)
                 e0.record()
-                ops.scaled_mm(a, w.t(), sa, sb, torch.bfloat16)
+                ops.scaled_mm(a, ws[0].t(), sa, sb, torch.bfloat16, out=y)
                 e1.record()
             torch.cuda.synchronize()
-            us = 1e3 * max_over_ranks(sum(e0.elapsed_time(e1) for e0, e1 in ev) / reps,
+            us = 1e3 * max_over_ranks(statistics.median(e0.elapsed_time(e1) for e0, e1 in ev),
                                       world, device)
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            flush.zero_()
+            torch.sum(clean, dim=0, out=sink)
+            s0.record()
+            for i in range(chain):
+                ops.scaled_mm(a, ws[i % copies].t(), sa, sb, torch.bfloat16, out=y)
+            s1.record()
+            torch.cuda.synchronize()
+            stream_us = 1e3 * max_over_ranks(s0.elapsed_time(s1) / chain, world, device)
             nbytes = m * k + n * k + 2 * m * n + 4 * m + 4 * n
             rows.append({"m": m, "n": n, "k": k, "tp": world, "us": round(us, 2),
                          "tops_per_gpu": round(2 * m * n * k / (us * 1e-6) / 1e12, 1),
-                         "hbm_gbs": round(nbytes / (us * 1e-6) / 1e9, 1)})
-            del a, sa
-        del w, sb
+                         "hbm_gbs": round(nbytes / (us * 1e-6) / 1e9, 1),
+                         "stream_us": round(stream_us, 2),
+                         "stream_hbm_gbs": round(nbytes / (stream_us * 1e-6) / 1e9, 1)})
+        del ws, sb, inputs
     return rows
 
 
@@ -383,6 +454,224 @@ def ulysses_send(device: torch.device, flush: torch.Tensor) -> list[dict]:
         rows.append(result)
         del a, sa
     return rows
+
+
+def _timed(fn, reps: int, flush: torch.Tensor, world: int, device) -> float:
+    """Median device time (ms) of ``fn`` over ``reps`` calls, L2 flushed before
+    each, barrier-separated, max over ranks."""
+    for _ in range(2):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(reps):
+        flush.zero_()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    return max_over_ranks(statistics.median(times), world, device)
+
+
+def multi_gpu_parity(mlp, world: int, rank: int, device, samples: int = 48) -> dict:
+    """One untimed fc2 of the timed step's operands through the reduce-scatter
+    path the bench ran (fused or NCCL) and through GEMM + NCCL, both compared
+    with the oracle on sampled rows of every owner block.
+
+    Oracle rows: each rank computes its bf16 partial of the sampled rows from
+    its own int8 activations and weight shard (exact int32 GEMM, fp32
+    epilogue), the ranks all-gather them, and each rank sums its owner rows in
+    rank order in fp32 and adds the bias -- the fused kernel's reduction order
+    (its bit-exactness is reported).  NCCL's ring rounds the running bf16 sum
+    at each hop, so its bar is wider.
+    """
+    from oracle import w8a8_oracle as orc
+    from taomate_hd_b200 import ops
+    from taomate_hd_b200.collectives import reduce_scatter_rows
+
+    rows = TOKENS // world
+    g = torch.Generator().manual_seed(4321)
+    idx = torch.cat([j * rows + torch.randperm(rows, generator=g)[:samples].sort().values
+                     for j in range(world)])
+    q = mlp.q2.q[idx.to(device)].cpu().numpy()
+    sa = mlp.q2.s[idx.to(device)].cpu().numpy().reshape(-1)
+    partial = orc.scaled_mm(q, mlp.fc2.q.cpu().numpy(), sa, mlp.fc2.scale.cpu().numpy(), None,
+                            torch.bfloat16)[0].to(device)
+    gathered = [torch.empty_like(partial) for _ in range(world)]
+    torch.distributed.all_gather(gathered, partial)
+    mine = slice(rank * samples, (rank + 1) * samples)
+    ref = torch.zeros(samples, D, dtype=torch.float32, device=device)
+    for r in range(world):
+        ref += gathered[r][mine].float()
+    ref = (ref + mlp.fc2.bias.float()).to(torch.bfloat16)
+    local = (idx[mine] - rank * rows).to(device)
+
+    out = torch.empty(rows, D, dtype=torch.bfloat16, device=device)
+    if mlp.peer is not None:
+        mlp.peer(mlp.q2.q, mlp.q2.s, mlp.fc2.q, mlp.fc2.scale, mlp.fc2.bias, out)
+        mlp.peer.check()
+        path = "fused"
+    else:
+        path = "nccl"
+    part = ops.scaled_mm(mlp.q2.q, mlp.fc2.q.t(), mlp.q2.s, mlp.fc2.scale.reshape(1, -1),
+                         torch.bfloat16, mlp.fc2.bias if rank == 0 else None)
+    nccl = reduce_scatter_rows(part, group=torch.distributed.group.WORLD, world_size=world)
+    if path == "nccl":
+        out = nccl
+    torch.cuda.synchronize()
+
+    def compare(y: torch.Tensor, tol: float) -> dict:
+        got = y[local].float()
+        d = (got - ref.float()).abs()
+        return {"max_abs": float(d.max()),
+                "max_rel": float((d / ref.float().abs().clamp_min(1e-2)).max()),
+                "bit_exact": bool(torch.equal(y[local].view(torch.int16), ref.view(torch.int16))),
+                "within_tol": bool(torch.allclose(got, ref.float(), atol=tol, rtol=tol))}
+
+    res_path = compare(out, 1e-2 if path == "fused" else 2e-2)
+    res_nccl = compare(nccl, 2e-2)
+    flag = torch.tensor([1 if res_path["within_tol"] else 0], dtype=torch.int32, device=device)
+    torch.distributed.all_reduce(flag, op=torch.distributed.ReduceOp.MIN)
+    exact = torch.tensor([1 if res_path["bit_exact"] else 0], dtype=torch.int32, device=device)
+    torch.distributed.all_reduce(exact, op=torch.distributed.ReduceOp.MIN)
+    return {"path": path, "rows_checked_per_rank": samples, "rank0": res_path,
+            "nccl_rank0": res_nccl, "ok": bool(flag.item()),
+            "bit_exact_all_ranks": bool(exact.item()),
+            "tolerance": "fused: atol 1e-2 + rtol 1e-2 vs oracle rows (bit-exactness reported); "
+                         "NCCL bf16 ring: 2e-2"}
+
+
+def reduce_vs_nccl(ctx, world: int, rank: int, device, flush: torch.Tensor) -> list[dict]:
+    """The row-parallel GEMM with its reduction, fused over NVLink against the
+    GEMM followed by NCCL, at this GPU count: 480p fc2 with a reduce-scatter
+    (8192 x 3072 x 12288 / t) and the 768p out-projection with an all-reduce
+    (20480 x 3072 x 3072 / t).  ``local_us`` is the GEMM alone (no reduction);
+    ``nvlink_gbs_fused`` counts the bytes that must leave each rank,
+    (t - 1) / t x M x N x 2 for the reduce-scatter and twice that for the
+    all-reduce."""
+    from taomate_hd_b200 import ops
+    from taomate_hd_b200.collectives import all_reduce_sum_inplace_, reduce_scatter_rows
+    from taomate_hd_b200.dit import row_weight
+    from taomate_hd_b200.peer_reduce import PeerAllReduce, PeerReduceScatter
+
+    out_rows = []
+    for name, m, n, k, mode in (("fc2_480p_reduce_scatter", TOKENS, D, FFN, "rs"),
+                                ("out_proj_768p_all_reduce", BLOCK_TOKENS, D, HEADS * HEAD_DIM,
+                                 "ar")):
+        kl = k // world
+        g = torch.Generator(device=device).manual_seed(99 + rank)
+        q = torch.randint(-127, 128, (m, kl), generator=g, device=device, dtype=torch.int8)
+        sa = torch.rand(m, 1, generator=g, device=device) * 1e-2 + 1e-4
+        w = row_weight(n, k, ctx, 7, device, bias=True)
+        partial = torch.empty(m, n, dtype=torch.bfloat16, device=device)
+        bias0 = w.bias if rank == 0 else None
+
+        def local():
+            ops.scaled_mm(q, w.q_t, sa, w.scale.reshape(1, -1), torch.bfloat16, bias0, out=partial)
+
+        row = {"name": name, "m": m, "n": n, "k_per_rank": kl, "tp": world,
+               "local_us": round(1e3 * _timed(local, 10, flush, world, device), 1)}
+        if world > 1:
+            rs_out = torch.empty(m // world, n, dtype=torch.bfloat16, device=device)
+            if mode == "rs":
+                peer = PeerReduceScatter(ctx, m, n, device)
+
+                def fused():
+                    peer(q, sa, w.q, w.scale, w.bias, rs_out)
+
+                def nccl():
+                    local()
+                    reduce_scatter_rows(partial, group=ctx.tp_group, world_size=world, out=rs_out)
+            else:
+                peer = PeerAllReduce(ctx, m, n, device)
+
+                def fused():
+                    peer(q, sa, w.q, w.scale, w.bias)
+
+                def nccl():
+                    local()
+                    all_reduce_sum_inplace_(partial, group=ctx.tp_group, world_size=world)
+            fused_ms = _timed(fused, 10, flush, world, device)
+            nccl_ms = _timed(nccl, 10, flush, world, device)
+            peer.check()
+            leave = (world - 1) / world * m * n * 2 * (1 if mode == "rs" else 2)
+            row.update(fused_us=round(1e3 * fused_ms, 1), gemm_nccl_us=round(1e3 * nccl_ms, 1),
+                       nvlink_gbs_fused=round(leave / (fused_ms * 1e-3) / 1e9, 1),
+                       bytes_leaving_rank=int(leave))
+            torch.cuda.synchronize()
+            barrier(world)
+            peer.close()
+        out_rows.append(row)
+        del q, sa, w, partial
+        torch.cuda.empty_cache()
+    return out_rows
+
+
+def library_baselines(device, flush: torch.Tensor) -> dict:
+    """The library bars on this GPU, timed like our kernels: cuBLAS's int8 GEMM
+    (``torch._int_mm``, int32 out) alone and followed by the same fp32
+    dequant + bias (+ GELU) epilogue in torch, at the fc1 and fc2 shapes, next
+    to our GEMM on the same operands; and vLLM's ``scaled_int8_quant`` (the
+    reference's own quant op) next to ours at both activation shapes, when
+    vLLM's compiled ops load here."""
+    from taomate_hd_b200 import ops
+
+    g = torch.Generator(device=device).manual_seed(5)
+    out = {}
+    for name, m, n, k, gelu in (("fc1_480p", TOKENS, FFN, D, True),
+                                ("fc2_480p", TOKENS, D, FFN, False)):
+        a = torch.randint(-127, 128, (m, k), generator=g, device=device, dtype=torch.int8)
+        b = torch.randint(-127, 128, (n, k), generator=g, device=device, dtype=torch.int8)
+        sa = torch.rand(m, 1, generator=g, device=device) * 1e-3
+        sb = torch.rand(1, n, generator=g, device=device) * 1e-3
+        bias = (torch.randn(n, generator=g, device=device) * 0.01).to(torch.bfloat16)
+        y = torch.empty(m, n, dtype=torch.bfloat16, device=device)
+
+        def cublas():
+            z = (sa * (sb * torch._int_mm(a, b.t()).float()) + bias.float()).to(torch.bfloat16)
+            if gelu:
+                z = torch.nn.functional.gelu(z.float(), approximate="tanh").to(torch.bfloat16)
+            return z
+
+        def cublas_gemm_only():
+            return torch._int_mm(a, b.t())
+
+        def ours():
+            ops.scaled_mm(a, b.t(), sa, sb, torch.bfloat16, bias, gelu_tanh=gelu, out=y)
+
+        row = {}
+        for label, fn in (("ours_us", ours), ("cublas_int8_plus_torch_epilogue_us", cublas),
+                          ("cublas_int8_gemm_only_us", cublas_gemm_only)):
+            row[label] = round(1e3 * _timed(fn, 10, flush, 1, device), 1)
+        row["ours_tops"] = round(2 * m * n * k / (row["ours_us"] * 1e-6) / 1e12, 1)
+        row["cublas_gemm_only_tops"] = round(
+            2 * m * n * k / (row["cublas_int8_gemm_only_us"] * 1e-6) / 1e12, 1)
+        out[name] = row
+        del a, b, sa, sb, bias, y
+    try:
+        from vllm import _custom_ops as vllm_ops
+
+        vllm_quant = vllm_ops.scaled_int8_quant
+    except Exception as exc:  # vLLM's compiled ops may not load
+        vllm_quant = None
+        out["vllm_quant"] = f"unavailable: {type(exc).__name__}"
+    for cols in (D, FFN):
+        x = torch.randn(TOKENS, cols, generator=g, device=device).to(torch.bfloat16)
+        row = {"rows": TOKENS, "cols": cols,
+               "ours_us": round(1e3 * _timed(lambda: ops.scaled_int8_quant(x), 10, flush, 1,
+                                             device), 1)}
+        if vllm_quant is not None:
+            try:
+                row["vllm_us"] = round(1e3 * _timed(lambda: vllm_quant(x), 10, flush, 1, device), 1)
+            except Exception as exc:
+                row["vllm_us"] = f"failed: {type(exc).__name__}"
+        nbytes = TOKENS * cols * 3 + TOKENS * 4
+        row["ours_gbs"] = round(nbytes / (row["ours_us"] * 1e-6) / 1e9, 1)
+        out[f"quant_{TOKENS}x{cols}"] = row
+        del x
+    return out
 
 
 def run_ours(args) -> int:
@@ -501,43 +790,47 @@ def run_ours(args) -> int:
     barrier(world)
     e2e_ms = max_over_ranks(e_start.elapsed_time(e_end) / K, world, device)
 
+    parity = multi_gpu_parity(mlp, world, rank, device) if world > 1 else None
     mlp_peer = mlp.peer
     extras = {}
     if not args.no_extras:
         del mlp
         torch.cuda.empty_cache()
-        block = TPW8A8BlockChain(BLOCK_TOKENS, D, HEADS, HEAD_DIM, FFN, ctx, device, seed=7)
         xb = torch.randn(BLOCK_TOKENS, D, generator=g, device=device).to(torch.bfloat16)
-        for _ in range(3):
-            block.forward(xb)
-        torch.cuda.synchronize()
-        barrier(world)
-        reps = max(5, K // 2)
-        bs = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
-        be = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
-        for i in range(reps):
-            flush.zero_()
-            bs[i].record()
-            block.forward(xb)
-            be[i].record()
-        torch.cuda.synchronize()
-        barrier(world)
-        block_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(bs, be)) / reps, world, device)
-        block_ops = block.int8_ops
-        del block
-        torch.cuda.empty_cache()
+        chains = {}
+        for fused in ((False, True) if world > 1 else (False,)):
+            block = TPW8A8BlockChain(BLOCK_TOKENS, D, HEADS, HEAD_DIM, FFN, ctx, device, seed=7,
+                                     fused=fused)
+            chains["fused" if fused else "nccl"] = _timed(lambda: block.forward(xb),
+                                                          max(5, K // 2), flush, world, device)
+            block_ops = block.int8_ops
+            if fused:
+                block.attn.peer_ar.check()
+                block.mlp.peer_ar.check()
+                barrier(world)
+                block.attn.peer_ar.close()
+                block.mlp.peer_ar.close()
+            del block
+            torch.cuda.empty_cache()
+        block_ms = min(chains.values())
         lora_stack = lora_block_stack(ctx, device, g, world, flush)
         torch.cuda.empty_cache()
+        reductions = reduce_vs_nccl(ctx, world, rank, device, flush)
         sweep = skinny_sweep(world, device, flush)
         ulysses = ulysses_send(device, flush) if world == 1 else None
+        libs = library_baselines(device, flush) if world == 1 else None
         extras = {"ms_per_768p_block_linear_chain": block_ms,
                   "block_768p_tops": block_ops / (block_ms * 1e-3) / 1e12,
+                  "block_768p_chain_ms": chains,
                   "block_768p_config": f"M={BLOCK_TOKENS}, d={D}, QKV N={3 * HEADS * HEAD_DIM}, "
                                        f"out-proj, fc1 N={FFN} (+GELU), fc2; all-reduce after "
-                                       f"row-parallel linears; no LoRA / modulate fusion",
+                                       "each row-parallel linear (fused over NVLink or NCCL; "
+                                       "the line's ms is the faster); no LoRA / modulate fusion",
                   "lora_block_stack_768p": lora_stack,
+                  "reduce_vs_nccl": reductions,
                   "skinny_sweep": sweep,
-                  "ulysses_send_768p": ulysses}
+                  "ulysses_send_768p": ulysses,
+                  "library_baselines": libs}
 
     if rank == 0:
         peaks = load_peaks()
@@ -545,9 +838,10 @@ def run_ours(args) -> int:
         per_launch_ops = 2 * TOKENS * D * (FFN // world)
         achieved = per_launch_ops / (gemm_avg * 1e-3) / 1e12
         traffic = ncu_traffic_per_launch("gemm_i8_pair_mlp480p.md") if world == 1 else None
-        cpu_base = None
+        cpu_base = cpu_bf16 = None
         if world == 1 and not args.no_cpu_baseline:
             cpu_base = time_cpu_reference(rows=512, min_seconds=10.0, max_passes=40)
+            cpu_bf16 = time_cpu_bf16_linear(rows=512, min_seconds=5.0, max_passes=20)
         line = {
             "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world, "steps": K,
             "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True,
@@ -585,14 +879,20 @@ def run_ours(args) -> int:
             "wall_s_timed_region": wall,
             "extras": extras,
         }
+        if parity is not None:
+            line["parity"] = parity
         if cpu_base is not None:
             line["cpu_baseline"] = cpu_base
+            line["cpu_baseline_bf16_linear"] = cpu_bf16
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.barrier()
         if mlp_peer is not None:
             mlp_peer.close()
         torch.distributed.destroy_process_group()
+    if parity is not None and not parity["ok"]:
+        print("parity check failed: the reduced fc2 rows differ from the oracle", file=sys.stderr)
+        return 1
     return 0
 
 

@@ -98,6 +98,10 @@ struct GemmArgs {
   // (sharing their ingress), and each rank would alternate between local
   // writes and pushes.
   int m_owners, mb_per_owner;
+  // Raster for long K (group_n > 0): tiles in groups of group_n N-blocks
+  // spanning every M-block, N fastest; see tile_coords.  0 = groups of
+  // kGroupM M-blocks, M fastest.
+  int group_n;
   uint32_t uses;  // 1-based count of calls made with this buffer set
   const __nv_bfloat16* red_bias;
   __nv_bfloat16* red_out;
@@ -113,15 +117,32 @@ struct GemmArgs {
   __nv_bfloat16* peer_out[kMaxPeers];
 };
 
+// Raster order of output tiles.  Concurrent tiles should share operand
+// panels in L2.  Default: groups of kGroupM M-blocks, M fastest -- a wave
+// shares kGroupM A panels and a few B panels.  With group_n > 0 (long K,
+// where kGroupM A panels of K bytes per row would not stay in L2 beside B):
+// groups of group_n N-blocks over all M-blocks, N fastest -- a wave shares
+// a few A panels, each read from DRAM once, while the group's B panels stay
+// resident for every M-block.
 __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb,
-                                            int m_owners, int mb_per_owner) {
-  const int group_size = kGroupM * num_n;
-  const int group = tile / group_size;
-  const int first_m = group * kGroupM;
-  const int gm = min(num_m - first_m, kGroupM);
-  const int local = tile - group * group_size;
-  mb = first_m + local % gm;
-  nb = local / gm;
+                                            int m_owners, int mb_per_owner, int group_n = 0) {
+  if (group_n > 0) {
+    const int group_size = group_n * num_m;
+    const int group = tile / group_size;
+    const int first_n = group * group_n;
+    const int gn = min(num_n - first_n, group_n);
+    const int local = tile - group * group_size;
+    nb = first_n + local % gn;
+    mb = local / gn;
+  } else {
+    const int group_size = kGroupM * num_n;
+    const int group = tile / group_size;
+    const int first_m = group * kGroupM;
+    const int gm = min(num_m - first_m, kGroupM);
+    const int local = tile - group * group_size;
+    mb = first_m + local % gm;
+    nb = local / gm;
+  }
   if (m_owners > 1) {  // num_m == m_owners x mb_per_owner
     const int owner = mb % m_owners;
     mb = owner * mb_per_owner + mb / m_owners;
@@ -996,7 +1017,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int kb0 = (unit - tile * g.splits) * g.kb_per_split;
         const int kb1 = min(kb0 + g.kb_per_split, g.kblocks);
         int mb, nb;
-        tile_coords(tile, g.num_m, g.num_n, mb, nb, g.m_owners, g.mb_per_owner);
+        tile_coords(tile, g.num_m, g.num_n, mb, nb, g.m_owners, g.mb_per_owner, g.group_n);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&bar.empty[stage], phase ^ 1u, bar.abort_flag, g.status)) {
             ok = false;
@@ -1087,14 +1108,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     ColPrefetch pf{};
     if (g.tma_store && static_cast<int>(blockIdx.x) < units) {
       int mb0, nb0;
-      tile_coords(static_cast<int>(blockIdx.x), g.num_m, g.num_n, mb0, nb0, g.m_owners, g.mb_per_owner);
+      tile_coords(static_cast<int>(blockIdx.x), g.num_m, g.num_n, mb0, nb0, g.m_owners, g.mb_per_owner, g.group_n);
       pf = col_prefetch<OutT>(g, nb0 * BN + epi_h * kHalf, kHalf,
                               static_cast<int64_t>(mb0) * kBM + epi_row, lane);
     }
     for (int unit = blockIdx.x; unit < units; unit += gridDim.x) {
       const int tile = unit / g.splits;
       int mb, nb;
-      tile_coords(tile, g.num_m, g.num_n, mb, nb, g.m_owners, g.mb_per_owner);
+      tile_coords(tile, g.num_m, g.num_n, mb, nb, g.m_owners, g.mb_per_owner, g.group_n);
       float sa_tile = 0.f;
       if (g.tma_store) {
         col_cache_store(stage, pf, kHalf, lane);
@@ -1103,7 +1124,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int next = unit + static_cast<int>(gridDim.x);
         if (next < units) {
           int mb1, nb1;
-          tile_coords(next, g.num_m, g.num_n, mb1, nb1, g.m_owners, g.mb_per_owner);
+          tile_coords(next, g.num_m, g.num_n, mb1, nb1, g.m_owners, g.mb_per_owner, g.group_n);
           pf = col_prefetch<OutT>(g, nb1 * BN + epi_h * kHalf, kHalf,
                                   static_cast<int64_t>(mb1) * kBM + epi_row, lane);
         }
@@ -1223,7 +1244,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int tile = pair; ok && tile < tiles; tile += pairs) {
         int mb, nb;
-        tile_coords(tile, g.num_m, g.num_n, mb, nb, g.m_owners, g.mb_per_owner);
+        tile_coords(tile, g.num_m, g.num_n, mb, nb, g.m_owners, g.mb_per_owner, g.group_n);
         const int a_row = mb * 2 * kBM + static_cast<int>(rank) * kBM;
         const int b_row = nb * BN + static_cast<int>(rank) * kBNHalf;
         for (int kb = 0; kb < g.kblocks; ++kb) {
@@ -1322,13 +1343,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     ColPrefetch pf{};
     if (g.tma_store && pair < tiles) {
       int mb0, nb0;
-      tile_coords(pair, g.num_m, g.num_n, mb0, nb0, g.m_owners, g.mb_per_owner);
+      tile_coords(pair, g.num_m, g.num_n, mb0, nb0, g.m_owners, g.mb_per_owner, g.group_n);
       pf = col_prefetch<OutT>(g, nb0 * BN + epi_h * kHalf, kHalf,
                               static_cast<int64_t>(mb0) * 2 * kBM + epi_row, lane);
     }
     for (int tile = pair; tile < tiles; tile += pairs) {
       int mb, nb;
-      tile_coords(tile, g.num_m, g.num_n, mb, nb, g.m_owners, g.mb_per_owner);
+      tile_coords(tile, g.num_m, g.num_n, mb, nb, g.m_owners, g.mb_per_owner, g.group_n);
       float sa_tile = 0.f;
       if (g.tma_store) {
         col_cache_store(stage, pf, kHalf, lane);
@@ -1336,7 +1357,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (tile + pairs < tiles) {
           int mb1, nb1;
-          tile_coords(tile + pairs, g.num_m, g.num_n, mb1, nb1, g.m_owners, g.mb_per_owner);
+          tile_coords(tile + pairs, g.num_m, g.num_n, mb1, nb1, g.m_owners, g.mb_per_owner, g.group_n);
           pf = col_prefetch<OutT>(g, nb1 * BN + epi_h * kHalf, kHalf,
                                   static_cast<int64_t>(mb1) * 2 * kBM + epi_row, lane);
         }
@@ -1574,7 +1595,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t lora_full_leader = map_to_cta(smem_u32(lora_full), 0);
       for (int tile = pair; ok && tile < tiles; tile += pairs) {
         int mb, nb;
-        tile_coords(tile, g.num_m, g.num_n, mb, nb, g.m_owners, g.mb_per_owner);
+        tile_coords(tile, g.num_m, g.num_n, mb, nb, g.m_owners, g.mb_per_owner, g.group_n);
         const int a_row = mb * 2 * kBM + static_cast<int>(rank) * kBM;
         const int b_row = nb * BN + static_cast<int>(rank) * kBNHalf;
         for (int kb = 0; kb < g.kblocks; ++kb) {
@@ -1723,19 +1744,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     ColPrefetch pf{};
     if (pair < tiles) {
       int mb0, nb0;
-      tile_coords(pair, g.num_m, g.num_n, mb0, nb0, g.m_owners, g.mb_per_owner);
+      tile_coords(pair, g.num_m, g.num_n, mb0, nb0, g.m_owners, g.mb_per_owner, g.group_n);
       pf = col_prefetch<OutT>(g, nb0 * BN + h * kBNHalf, kBNHalf,
                               static_cast<int64_t>(mb0) * 2 * kBM + epi_row, lane);
     }
     for (int tile = pair; tile < tiles; tile += pairs) {
       int mb, nb;
-      tile_coords(tile, g.num_m, g.num_n, mb, nb, g.m_owners, g.mb_per_owner);
+      tile_coords(tile, g.num_m, g.num_n, mb, nb, g.m_owners, g.mb_per_owner, g.group_n);
       col_cache_store(region, pf, kBNHalf, lane);
       const float sa_tile = pf.sa;
       __syncwarp();
       if (tile + pairs < tiles) {
         int mb1, nb1;
-        tile_coords(tile + pairs, g.num_m, g.num_n, mb1, nb1, g.m_owners, g.mb_per_owner);
+        tile_coords(tile + pairs, g.num_m, g.num_n, mb1, nb1, g.m_owners, g.mb_per_owner, g.group_n);
         pf = col_prefetch<OutT>(g, nb1 * BN + h * kBNHalf, kBNHalf,
                                 static_cast<int64_t>(mb1) * 2 * kBM + epi_row, lane);
       }
@@ -1803,6 +1824,21 @@ bool encode_out_map(CUtensorMap* map, GemmArgs& args) {
                         32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
 }
 
+// Raster choice (GemmArgs::group_n).  Once kGroupM A panels (rows_per_mb x K
+// bytes each) pass kAGroupBudget they no longer stay in L2 next to the B
+// panels a wave reads (the 480p fc2, K = 12288: 16 x 3 MiB of A), so the
+// tiles switch to N-fastest groups whose B panels fit kBGroupBudget.
+constexpr uint64_t kAGroupBudget = 24ull << 20;
+constexpr uint64_t kBGroupBudget = 48ull << 20;
+
+int choose_group_n(int num_n, int rows_per_mb, int bn, int k) {
+  const uint64_t a_group = static_cast<uint64_t>(kGroupM) * rows_per_mb * static_cast<uint64_t>(k);
+  if (a_group <= kAGroupBudget) return 0;
+  const uint64_t b_panel = static_cast<uint64_t>(bn) * static_cast<uint64_t>(k);
+  const uint64_t fit = b_panel > 0 ? kBGroupBudget / b_panel : 1;
+  return static_cast<int>(fit < 1 ? 1 : (fit > static_cast<uint64_t>(num_n) ? num_n : fit));
+}
+
 template <int BN, int STAGES, typename OutT>
 int launch_single(const Operands& op, GemmArgs args, int sms, cudaStream_t stream) {
   using L = Smem<BN, STAGES>;
@@ -1810,6 +1846,7 @@ int launch_single(const Operands& op, GemmArgs args, int sms, cudaStream_t strea
   args.num_n = (args.N + BN - 1) / BN;
   args.m_owners = args.world;
   args.mb_per_owner = args.world > 0 ? args.rows_per_owner / kBM : 0;
+  args.group_n = choose_group_n(args.num_n, kBM, BN, args.K);
   CUtensorMap ta, tb;
   if (!encode_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, op.a, args.K, args.M, op.lda, kBK, kBM,
                       CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -1846,6 +1883,7 @@ int launch_pair(const Operands& op, GemmArgs args, int max_pairs, cudaStream_t s
   args.num_n = (args.N + BN - 1) / BN;
   args.m_owners = args.world;
   args.mb_per_owner = args.world > 0 ? args.rows_per_owner / (2 * kBM) : 0;
+  args.group_n = choose_group_n(args.num_n, 2 * kBM, BN, args.K);
   CUtensorMap ta, tb;
   if (!encode_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, op.a, args.K, args.M, op.lda, kBK, kBM,
                       CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -1896,6 +1934,7 @@ int launch_pair_lora(const Operands& op, GemmArgs args, const LoraSpec& lora, in
   using L = LoraSmem<kStages>;
   args.num_m = (args.M + 2 * kBM - 1) / (2 * kBM);
   args.num_n = (args.N + 255) / 256;
+  args.group_n = choose_group_n(args.num_n, 2 * kBM, 256, args.K);
   args.tma_store = 1;
   const CUtensorMapDataType dt = std::is_same<OutT, __nv_bfloat16>::value
                                      ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16

@@ -226,15 +226,24 @@ def test_ops_module_passes_the_reference_backend_check():
         assert callable(getattr(namespace, name, None)), name
 
 
-def _tile_coords(tile, num_m, num_n, m_owners, mb_per_owner, group_m=16):
-    """Restatement of the GEMM's tile_coords (grouped raster, then the
-    owner-interleaved M order of the fused reduce-scatter / all-reduce)."""
-    group_size = group_m * num_n
-    group = tile // group_size
-    first_m = group * group_m
-    gm = min(num_m - first_m, group_m)
-    local = tile - group * group_size
-    mb, nb = first_m + local % gm, local // gm
+def _tile_coords(tile, num_m, num_n, m_owners, mb_per_owner, group_m=16, group_n=0):
+    """Restatement of the GEMM's tile_coords (grouped raster: M-block groups,
+    or N-block groups for long K; then the owner-interleaved M order of the
+    fused reduce-scatter / all-reduce)."""
+    if group_n > 0:
+        group_size = group_n * num_m
+        group = tile // group_size
+        first_n = group * group_n
+        gn = min(num_n - first_n, group_n)
+        local = tile - group * group_size
+        mb, nb = local // gn, first_n + local % gn
+    else:
+        group_size = group_m * num_n
+        group = tile // group_size
+        first_m = group * group_m
+        gm = min(num_m - first_m, group_m)
+        local = tile - group * group_size
+        mb, nb = first_m + local % gm, local // gm
     if m_owners > 1:
         mb = (mb % m_owners) * mb_per_owner + mb // m_owners
     return mb, nb
@@ -300,3 +309,32 @@ def test_ulysses_errors_match_reference_before_any_launch():
         merged_qkv_sequence_to_heads_w8a8(q, s, w, ws, None, num_heads=4, head_dim=128, world=2)
     with pytest.raises(RuntimeError, match="initialized torch.distributed"):
         exchange_qkv(torch.zeros(2, 3, 4, 2, 8, dtype=torch.bfloat16))
+
+
+def _choose_group_n(num_n, rows_per_mb, bn, k, group_m=16):
+    """Restatement of the host's choose_group_n (24 MiB of A panels, 48 MiB of B)."""
+    if group_m * rows_per_mb * k <= 24 << 20:
+        return 0
+    return max(1, min(num_n, (48 << 20) // (bn * k)))
+
+
+@pytest.mark.parametrize("m,n,k,rows_per_mb,bn,world", [
+    (8192, 3072, 12288, 256, 256, 0),    # 480p fc2 at TP=1: N-fastest groups
+    (8192, 3072, 12288, 256, 256, 2),    # owner interleave on top
+    (8192, 3072, 6144, 256, 256, 2),     # fc2 at TP=2: 24 MiB of A panels, M-groups
+    (20480, 12288, 12288, 256, 256, 0),  # B does not fit: groups of a few N-blocks
+    (8192, 12288, 3072, 256, 256, 0),    # fc1: short K keeps M-groups
+    (1000, 3000, 16384, 128, 64, 0),     # ragged M and N
+])
+def test_long_k_raster_is_a_permutation(m, n, k, rows_per_mb, bn, world):
+    num_m, num_n = -(-m // rows_per_mb), -(-n // bn)
+    group_n = _choose_group_n(num_n, rows_per_mb, bn, k)
+    assert (group_n == 0) == (k <= 6144)
+    mb_per_owner = num_m // world if world else 0
+    tiles = [_tile_coords(t, num_m, num_n, world, mb_per_owner, group_n=group_n)
+             for t in range(num_m * num_n)]
+    assert sorted(tiles) == [(a, b) for a in range(num_m) for b in range(num_n)]
+    if group_n:
+        # a wave of 74 pair tiles touches few A panels and stays in one N-group
+        wave = tiles[:74]
+        assert len({mb for mb, _ in wave}) <= -(-74 // min(group_n, num_n)) + 1
