@@ -37,4 +37,27 @@ inline int check_launch() {
   return cudaGetLastError() == cudaSuccess ? TM_OK : TM_ERR_CUDA;
 }
 
+// Launch with programmatic dependent launch allowed (the kernel calls
+// griddep_wait before reading global data): `attrs` are the launch's other
+// attributes.  Should the driver refuse the combination, the launch is
+// repeated without it (the kernel's griddep_wait is then a no-op).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_with_pdl(cudaLaunchConfig_t cfg, const cudaLaunchAttribute* attrs, int nattrs,
+                            void (*kernel)(KArgs...), Args&&... args) {
+  cudaLaunchAttribute all[4];
+  int n = 0;
+  for (int i = 0; i < nattrs && n < 3; ++i) all[n++] = attrs[i];
+  all[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  all[n].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = all;
+  cfg.numAttrs = static_cast<unsigned>(n + 1);
+  cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, args...);
+  if (err != cudaSuccess) {
+    cudaGetLastError();
+    cfg.numAttrs = static_cast<unsigned>(n);
+    err = cudaLaunchKernelEx(&cfg, kernel, args...);
+  }
+  return err;
+}
+
 }  // namespace tmw

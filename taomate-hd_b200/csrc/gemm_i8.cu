@@ -964,6 +964,19 @@ __device__ __forceinline__ uint8_t* align1k(uint8_t* p) {
                                     ~static_cast<uintptr_t>(1023));
 }
 
+// Before a kernel waits for its predecessor on the stream (programmatic
+// dependent launch), its producer pulls the weight rows of its first tile
+// towards L2: weights are never written by the kernel before, so the reads
+// can overlap that kernel's tail.  With few M tiles (skinny token counts, a
+// weight-bound GEMM) the whole K range is requested; otherwise only the
+// k-blocks the pipeline fills first, since many CTAs share each panel.
+template <int STAGES>
+__device__ __forceinline__ void prefetch_weight_panel(const CUtensorMap* tm_b, const GemmArgs& g,
+                                                      int kb0, int kb1, int b_row) {
+  const int count = g.num_m <= 2 ? kb1 - kb0 : min(kb1 - kb0, STAGES);
+  for (int i = 0; i < count; ++i) tma_prefetch_l2_2d(tm_b, (kb0 + i) * kBK, b_row);
+}
+
 // ====================================================================== one CTA
 template <int BN, int STAGES, typename OutT>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -996,6 +1009,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tm_a);
     tma_prefetch_desc(&tm_b);
     if (g.tma_store) tma_prefetch_desc(&tm_out);
+    if (static_cast<int>(blockIdx.x) < units) {
+      const int tile = blockIdx.x / g.splits;
+      const int kb0 = (blockIdx.x - tile * g.splits) * g.kb_per_split;
+      const int kb1 = min(kb0 + g.kb_per_split, g.kblocks);
+      int mb, nb;
+      tile_coords(tile, g.num_m, g.num_n, mb, nb, g.m_owners, g.mb_per_owner, g.group_n);
+      prefetch_weight_panel<STAGES>(&tm_b, g, kb0, kb1, nb * BN);
+    }
   }
   if (warp == 1) {
     tmem_alloc(bar.tmem_slot, 2 * BN);
@@ -1005,6 +1026,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *bar.tmem_slot;
+  griddep_wait();
+  griddep_launch_dependents();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -1226,6 +1249,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tm_a);
     tma_prefetch_desc(&tm_b);
     if (g.tma_store) tma_prefetch_desc(&tm_out);
+    if (pair < tiles) {
+      int mb, nb;
+      tile_coords(pair, g.num_m, g.num_n, mb, nb, g.m_owners, g.mb_per_owner, g.group_n);
+      prefetch_weight_panel<STAGES>(&tm_b, g, 0, g.kblocks,
+                                    nb * BN + static_cast<int>(rank) * kBNHalf);
+    }
   }
   if (warp == 1) {
     tmem_alloc_pair(bar.tmem_slot, PairTmem<BN>::kCols);
@@ -1235,6 +1264,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
   tc_fence_after();
   const uint32_t tmem_base = *bar.tmem_slot;
+  griddep_wait();
+  griddep_launch_dependents();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -1576,6 +1607,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tm_out);
     tma_prefetch_desc(&tm_lt);
     tma_prefetch_desc(&tm_lb);
+    if (pair < tiles) {
+      int mb, nb;
+      tile_coords(pair, g.num_m, g.num_n, mb, nb, g.m_owners, g.mb_per_owner, g.group_n);
+      prefetch_weight_panel<STAGES>(&tm_b, g, 0, g.kblocks,
+                                    nb * BN + static_cast<int>(rank) * kBNHalf);
+    }
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, 512);
@@ -1585,6 +1622,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_wait();
+  griddep_launch_dependents();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -1872,7 +1911,9 @@ int launch_single(const Operands& op, GemmArgs args, int sms, cudaStream_t strea
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = args.world > 0 ? 1 : 0;
-  if (cudaLaunchKernelEx(&cfg, kernel, ta, tb, to, args) != cudaSuccess) return TM_ERR_CUDA;
+  const cudaError_t err = args.world > 0 ? cudaLaunchKernelEx(&cfg, kernel, ta, tb, to, args)
+                                         : launch_with_pdl(cfg, attr, 0, kernel, ta, tb, to, args);
+  if (err != cudaSuccess) return TM_ERR_CUDA;
   return check_launch();
 }
 
@@ -1914,7 +1955,9 @@ int launch_pair(const Operands& op, GemmArgs args, int max_pairs, cudaStream_t s
   attr[1].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = args.world > 0 ? 2 : 1;
-  if (cudaLaunchKernelEx(&cfg, kernel, ta, tb, to, args) != cudaSuccess) return TM_ERR_CUDA;
+  const cudaError_t err = args.world > 0 ? cudaLaunchKernelEx(&cfg, kernel, ta, tb, to, args)
+                                         : launch_with_pdl(cfg, attr, 1, kernel, ta, tb, to, args);
+  if (err != cudaSuccess) return TM_ERR_CUDA;
   return check_launch();
 }
 
@@ -1969,9 +2012,7 @@ int launch_pair_lora(const Operands& op, GemmArgs args, const LoraSpec& lora, in
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, kernel, ta, tb, to, tlt, tlb, args) != cudaSuccess)
+  if (launch_with_pdl(cfg, attr, 1, kernel, ta, tb, to, tlt, tlb, args) != cudaSuccess)
     return TM_ERR_CUDA;
   return check_launch();
 }

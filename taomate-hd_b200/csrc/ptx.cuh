@@ -113,6 +113,22 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, 
   }
 }
 
+// ---------------------------------------------------------------- dependent launch
+// Programmatic dependent launch (kernels launched with the
+// programmatic-stream-serialization attribute): griddep_wait blocks until the
+// grid before this one on the stream has completed and its writes are
+// visible (a no-op when there is none), so every read of data that grid may
+// have written comes after it; griddep_launch_dependents lets the next grid
+// be scheduled -- on SMs this grid leaves free, its prologue overlapping this
+// grid's work -- once every CTA here has issued it or exited.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -127,6 +143,15 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* ba
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
+}
+
+// Prefetch one tile of a tensor map into L2 (no shared memory, no
+// completion to wait for).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
 }
 
 // 2-D tiled bulk tensor store shared -> global, tracked by this thread's bulk

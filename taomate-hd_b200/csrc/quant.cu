@@ -20,6 +20,7 @@
 #include <type_traits>
 
 #include "common.h"
+#include "ptx.cuh"
 
 namespace tmw {
 namespace {
@@ -422,6 +423,8 @@ template <typename T, int VPT, int MODE>
 __global__ void __launch_bounds__(256, (quant_min_blocks<MODE, VPT>())) quant_rows_kernel(
     const QuantParams p) {
   constexpr int E = VecTraits<T>::kElems;
+  griddep_wait();  // the rows may come from the previous kernel on the stream
+  griddep_launch_dependents();
   __shared__ double red_f64[8];  // the RMSNorm sum; also 8 floats for the maxima
   float* red = reinterpret_cast<float*>(red_f64);
   const int tpr = 1 << p.tpr_log2;
@@ -558,6 +561,8 @@ __global__ void __launch_bounds__(256, (quant_min_blocks<MODE, VPT>())) quant_ro
 // Two-pass scalar fallback: any width, any alignment.  One block per row.
 template <typename T, int MODE>
 __global__ void __launch_bounds__(256) quant_rows_scalar_kernel(const QuantParams p) {
+  griddep_wait();
+  griddep_launch_dependents();
   __shared__ float red[8];
   const int64_t row = blockIdx.x;
   if (row >= p.rows) return;
@@ -625,19 +630,23 @@ int launch_vec(const QuantParams& base, int tpr_log2, int vpt, cudaStream_t stre
   const int rpb = 256 >> tpr_log2;
   const int64_t grid = (p.rows + rpb - 1) / rpb;
   if (grid > 0x7fffffffLL) return TM_ERR_TOO_LARGE;
-  const dim3 g(static_cast<unsigned>(grid));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cudaError_t err;
   switch (round_vpt(vpt)) {
-    case 1: quant_rows_kernel<T, 1, MODE><<<g, 256, 0, stream>>>(p); break;
-    case 2: quant_rows_kernel<T, 2, MODE><<<g, 256, 0, stream>>>(p); break;
-    case 3: quant_rows_kernel<T, 3, MODE><<<g, 256, 0, stream>>>(p); break;
-    case 4: quant_rows_kernel<T, 4, MODE><<<g, 256, 0, stream>>>(p); break;
-    case 6: quant_rows_kernel<T, 6, MODE><<<g, 256, 0, stream>>>(p); break;
-    case 8: quant_rows_kernel<T, 8, MODE><<<g, 256, 0, stream>>>(p); break;
-    case 12: quant_rows_kernel<T, 12, MODE><<<g, 256, 0, stream>>>(p); break;
-    case 16: quant_rows_kernel<T, 16, MODE><<<g, 256, 0, stream>>>(p); break;
+    case 1: err = launch_with_pdl(cfg, nullptr, 0, quant_rows_kernel<T, 1, MODE>, p); break;
+    case 2: err = launch_with_pdl(cfg, nullptr, 0, quant_rows_kernel<T, 2, MODE>, p); break;
+    case 3: err = launch_with_pdl(cfg, nullptr, 0, quant_rows_kernel<T, 3, MODE>, p); break;
+    case 4: err = launch_with_pdl(cfg, nullptr, 0, quant_rows_kernel<T, 4, MODE>, p); break;
+    case 6: err = launch_with_pdl(cfg, nullptr, 0, quant_rows_kernel<T, 6, MODE>, p); break;
+    case 8: err = launch_with_pdl(cfg, nullptr, 0, quant_rows_kernel<T, 8, MODE>, p); break;
+    case 12: err = launch_with_pdl(cfg, nullptr, 0, quant_rows_kernel<T, 12, MODE>, p); break;
+    case 16: err = launch_with_pdl(cfg, nullptr, 0, quant_rows_kernel<T, 16, MODE>, p); break;
     default: return TM_ERR_UNSUPPORTED;
   }
-  return check_launch();
+  return err == cudaSuccess ? check_launch() : TM_ERR_CUDA;
 }
 
 template <typename T, int MODE>
@@ -648,7 +657,12 @@ int launch_quant_typed(const QuantParams& p, cudaStream_t stream) {
                       aligned16(p.q) && pick_layout(p.cols / E, &tpr_log2, &vpt);
   if (vec_ok) return launch_vec<T, MODE>(p, tpr_log2, vpt, stream);
   if (p.rows > 0x7fffffffLL) return TM_ERR_TOO_LARGE;
-  quant_rows_scalar_kernel<T, MODE><<<static_cast<unsigned>(p.rows), 256, 0, stream>>>(p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(p.rows));
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  if (launch_with_pdl(cfg, nullptr, 0, quant_rows_scalar_kernel<T, MODE>, p) != cudaSuccess)
+    return TM_ERR_CUDA;
   return check_launch();
 }
 
