@@ -485,7 +485,10 @@ def multi_gpu_parity(mlp, world: int, rank: int, device, samples: int = 48) -> d
     epilogue), the ranks all-gather them, and each rank sums its owner rows in
     rank order in fp32 and adds the bias -- the fused kernel's reduction order
     (its bit-exactness is reported).  NCCL's ring rounds the running bf16 sum
-    at each hop, so its bar is wider.
+    at each hop, so where terms cancel it can be far off in relative terms;
+    its bar is the rounding bound: at most world + 2 roundings of 2^-8 (bf16's
+    unit roundoff) of the magnitudes involved,
+    |y - ref| <= (world + 2) 2^-8 (sum |partial| + |bias| + |ref|).
     """
     from oracle import w8a8_oracle as orc
     from taomate_hd_b200 import ops
@@ -506,6 +509,10 @@ def multi_gpu_parity(mlp, world: int, rank: int, device, samples: int = 48) -> d
     for r in range(world):
         ref += gathered[r][mine].float()
     ref = (ref + mlp.fc2.bias.float()).to(torch.bfloat16)
+    mag = torch.zeros(samples, D, dtype=torch.float32, device=device)
+    for r in range(world):
+        mag += gathered[r][mine].float().abs()
+    ring_bound = (world + 2) * 2.0 ** -8 * (mag + mlp.fc2.bias.float().abs() + ref.float().abs())
     local = (idx[mine] - rank * rows).to(device)
 
     out = torch.empty(rows, D, dtype=torch.bfloat16, device=device)
@@ -522,16 +529,18 @@ def multi_gpu_parity(mlp, world: int, rank: int, device, samples: int = 48) -> d
         out = nccl
     torch.cuda.synchronize()
 
-    def compare(y: torch.Tensor, tol: float) -> dict:
+    def compare(y: torch.Tensor, ring: bool) -> dict:
         got = y[local].float()
         d = (got - ref.float()).abs()
+        ok = (bool((d <= ring_bound).all()) if ring
+              else bool(torch.allclose(got, ref.float(), atol=1e-2, rtol=1e-2)))
         return {"max_abs": float(d.max()),
                 "max_rel": float((d / ref.float().abs().clamp_min(1e-2)).max()),
                 "bit_exact": bool(torch.equal(y[local].view(torch.int16), ref.view(torch.int16))),
-                "within_tol": bool(torch.allclose(got, ref.float(), atol=tol, rtol=tol))}
+                "within_tol": ok}
 
-    res_path = compare(out, 1e-2 if path == "fused" else 2e-2)
-    res_nccl = compare(nccl, 2e-2)
+    res_path = compare(out, ring=path == "nccl")
+    res_nccl = compare(nccl, ring=True)
     flag = torch.tensor([1 if res_path["within_tol"] else 0], dtype=torch.int32, device=device)
     torch.distributed.all_reduce(flag, op=torch.distributed.ReduceOp.MIN)
     exact = torch.tensor([1 if res_path["bit_exact"] else 0], dtype=torch.int32, device=device)
@@ -540,7 +549,7 @@ def multi_gpu_parity(mlp, world: int, rank: int, device, samples: int = 48) -> d
             "nccl_rank0": res_nccl, "ok": bool(flag.item()),
             "bit_exact_all_ranks": bool(exact.item()),
             "tolerance": "fused: atol 1e-2 + rtol 1e-2 vs oracle rows (bit-exactness reported); "
-                         "NCCL bf16 ring: 2e-2"}
+                         "NCCL bf16 ring: (world + 2) * 2^-8 * (sum |partial| + |bias| + |ref|)"}
 
 
 def reduce_vs_nccl(ctx, world: int, rank: int, device, flush: torch.Tensor) -> list[dict]:

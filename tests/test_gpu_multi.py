@@ -15,8 +15,12 @@ small shape and at the BASELINE shapes (480p fc2: 8192 x 3072 x 12288 / t;
   rows comes from the oracle's exact int32 GEMM and fp32 epilogue, the
   partials are summed in fp32 in rank order and the bias is added, the order
   the kernel uses, so the fused result must match bit for bit;
-* against NCCL's reduce-scatter / all-reduce of the same partials (bf16 ring
-  sums: within the bf16 tolerance).
+* against NCCL's reduce-scatter / all-reduce of the same partials.  NCCL
+  sums bf16 partials with a bf16 rounding after every step, so where terms
+  cancel its result can be far from the exact sum in relative terms; the
+  check is the rounding bound itself: at most world + 2 roundings, each off
+  by at most 2^-8 (bf16's unit roundoff) of the magnitudes involved, i.e.
+  |fused - nccl| <= (world + 2) * 2^-8 * (sum over ranks of |partial| + |fused|).
 
 The ranks run as child processes with NCCL's NVLS off; each world size is
 skipped on a box with fewer GPUs.
@@ -121,10 +125,15 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
                     # NCCL on the same partials (the bias once, from rank 0)
                     partial = ops.scaled_mm(q, wq.t(), s, ws.reshape(1, -1), torch.bfloat16,
                                             bias.to(device) if rank == 0 else None)
+                    mag = partial.abs().float()
                     if mode == "rs":
                         nccl = reduce_scatter_rows(partial, group=group, world_size=world)
+                        mag_sum = torch.empty(rows, n, dtype=torch.float32, device=device)
+                        torch.distributed.reduce_scatter_tensor(mag_sum, mag, group=group)
                     else:
                         nccl = all_reduce_sum(partial, group=group, world_size=world)
+                        mag_sum = mag
+                        torch.distributed.all_reduce(mag_sum, group=group)
                     torch.cuda.synchronize()
                     lo, hi = (rank * rows, (rank + 1) * rows) if mode == "rs" else (0, m)
                     idx = _sample_rows(lo, hi, 96, seed=call + m)
@@ -132,14 +141,17 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
                     got = y.cpu()[torch.from_numpy(idx - (lo if mode == "rs" else 0))]
                     exact = bool(torch.equal(got.view(torch.int16), ref.view(torch.int16)))
                     err = float((got.float() - ref.float()).abs().max())
-                    nccl_close = bool(torch.allclose(y.cpu().float(), nccl.cpu().float(),
-                                                     atol=2e-2, rtol=2e-2))
+                    yf = y.float()
+                    bound = (world + 2) * 2.0 ** -8 * (mag_sum + yf.abs())
+                    excess = (yf - nccl.float()).abs() / bound.clamp_min(1e-30)
+                    nccl_close = bool((excess <= 1.0).all())
+                    nccl_excess = float(excess.max())
                     kept = True
                     if mode == "ar" and prev is not None:
                         kept = bool(torch.equal(prev[0].cpu(), prev[1]))
                     if mode == "ar":
                         prev = (y, y.cpu().clone())
-                    checks.append((mode, m, n, k, call, exact, err, nccl_close, kept))
+                    checks.append((mode, m, n, k, call, exact, err, nccl_close, nccl_excess, kept))
                 peer.check()
                 peer.close()
         # Ulysses exchange of a merged QKV projection: the fused send layout
@@ -204,10 +216,10 @@ def test_fused_row_parallel_reductions(tmp_path, world):
         assert res["ok"], res.get("error")
         assert res["device_status"] == 0
         assert res["ulysses_ok"], f"rank {r}: Ulysses exchange differs from the reference path"
-        for (mode, m, n, k, call, exact, err, nccl_close, kept) in res["checks"]:
+        for (mode, m, n, k, call, exact, err, nccl_close, excess, kept) in res["checks"]:
             where = f"{mode} world {world} rank {r} {m}x{n}x{k} call {call}"
             assert exact, f"{where}: differs from the oracle (max abs {err})"
-            assert nccl_close, f"{where}: differs from the NCCL path"
+            assert nccl_close, f"{where}: differs from the NCCL path ({excess:.2f} x the bound)"
             assert kept, f"{where}: the previous call's output changed"
 
 
