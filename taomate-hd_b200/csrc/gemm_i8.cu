@@ -196,6 +196,23 @@ __device__ __forceinline__ float round_out<__half>(float v) {
   return __half2float(__float2half_rn(v));
 }
 
+// Round two values to OutT and back with one paired conversion (the same
+// bits as two round_out calls; the conversion unit, which bounds the
+// epilogue's arithmetic, does half the work for bf16).
+template <typename OutT>
+__device__ __forceinline__ void round2_out(float& a, float& b);
+template <>
+__device__ __forceinline__ void round2_out<__nv_bfloat16>(float& a, float& b) {
+  const uint32_t p = pack2<__nv_bfloat16>(a, b);  // a in the low half, b in the high half
+  a = __uint_as_float(p << 16);
+  b = __uint_as_float(p & 0xffff0000u);
+}
+template <>
+__device__ __forceinline__ void round2_out<__half>(float& a, float& b) {
+  a = round_out<__half>(a);
+  b = round_out<__half>(b);
+}
+
 // Dequantise 16 consecutive columns held in r[0..15] of one row and pack
 // them into two 16-byte words of OutT.  Columns past N are never stored.
 template <typename OutT>
@@ -236,12 +253,13 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& g, const uint32_t* r,
     }
   } else {
 #pragma unroll
-    for (int j = 0; j < 16; ++j)
-      y[j] = __fmul_rn(sa, __fmul_rn(sb[j], __int2float_rn(static_cast<int>(r[j]))));
+    for (int j = 0; j < 16; ++j) y[j] = __fmul_rn(sa, __fmul_rn(sb[j], __int2float_rn(static_cast<int>(r[j]))));
   }
   if (g.epilogue & TM_EPI_GELU_TANH) {
 #pragma unroll
-    for (int j = 0; j < 16; ++j) y[j] = gelu_tanh(round_out<OutT>(y[j]));
+    for (int j = 0; j < 16; j += 2) round2_out<OutT>(y[j], y[j + 1]);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) y[j] = gelu_tanh(y[j]);
   }
   o0.x = pack2<OutT>(y[0], y[1]);
   o0.y = pack2<OutT>(y[2], y[3]);
@@ -440,12 +458,13 @@ __device__ __forceinline__ void dequant16_cached(const GemmArgs& g, const uint32
     }
   } else {
 #pragma unroll
-    for (int j = 0; j < 16; ++j)
-      y[j] = __fmul_rn(sa, __fmul_rn(sb[j], __int2float_rn(static_cast<int>(r[j]))));
+    for (int j = 0; j < 16; ++j) y[j] = __fmul_rn(sa, __fmul_rn(sb[j], __int2float_rn(static_cast<int>(r[j]))));
   }
   if (g.epilogue & TM_EPI_GELU_TANH) {
 #pragma unroll
-    for (int j = 0; j < 16; ++j) y[j] = gelu_tanh(round_out<OutT>(y[j]));
+    for (int j = 0; j < 16; j += 2) round2_out<OutT>(y[j], y[j + 1]);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) y[j] = gelu_tanh(y[j]);
   }
   o0.x = pack2<OutT>(y[0], y[1]);
   o0.y = pack2<OutT>(y[2], y[3]);
@@ -1497,15 +1516,22 @@ __device__ __forceinline__ void lora_convert_in_place(const GemmArgs& g, uint32_
       for (int j = 0; j < 4; ++j) braw[j] = reinterpret_cast<const uint4*>(bias_s + c * 32)[j];
       const OutT* be = reinterpret_cast<const OutT*>(braw);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float x = __fmul_rn(sb[j], __int2float_rn(static_cast<int>(r[j])));
-        r[j] = __float_as_uint(round_out<OutT>(__fmaf_rn(sa, x, out_to_f32<OutT>(be[j]))));
+      for (int j = 0; j < 32; j += 2) {
+        float y0 = __fmaf_rn(sa, __fmul_rn(sb[j], __int2float_rn(static_cast<int>(r[j]))), out_to_f32<OutT>(be[j]));
+        float y1 = __fmaf_rn(sa, __fmul_rn(sb[j + 1], __int2float_rn(static_cast<int>(r[j + 1]))),
+                             out_to_f32<OutT>(be[j + 1]));
+        round2_out<OutT>(y0, y1);
+        r[j] = __float_as_uint(y0);
+        r[j + 1] = __float_as_uint(y1);
       }
     } else {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float x = __fmul_rn(sb[j], __int2float_rn(static_cast<int>(r[j])));
-        r[j] = __float_as_uint(round_out<OutT>(__fmul_rn(sa, x)));
+      for (int j = 0; j < 32; j += 2) {
+        float y0 = __fmul_rn(sa, __fmul_rn(sb[j], __int2float_rn(static_cast<int>(r[j]))));
+        float y1 = __fmul_rn(sa, __fmul_rn(sb[j + 1], __int2float_rn(static_cast<int>(r[j + 1]))));
+        round2_out<OutT>(y0, y1);
+        r[j] = __float_as_uint(y0);
+        r[j + 1] = __float_as_uint(y1);
       }
     }
     tmem_st_32x32b_x32(t_row + static_cast<uint32_t>(c * 32), r);
@@ -1526,9 +1552,12 @@ __device__ __forceinline__ void lora_store_tile(const GemmArgs& g, const CUtenso
     if (c == 3) release();
     float y[32];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      y[j] = __uint_as_float(r[j]);
-      if (g.epilogue & TM_EPI_GELU_TANH) y[j] = gelu_tanh(round_out<OutT>(y[j]));
+    for (int j = 0; j < 32; ++j) y[j] = __uint_as_float(r[j]);
+    if (g.epilogue & TM_EPI_GELU_TANH) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 2) round2_out<OutT>(y[j], y[j + 1]);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) y[j] = gelu_tanh(y[j]);
     }
     uint4 o[4];
 #pragma unroll
