@@ -805,6 +805,9 @@ def run_ours(args) -> int:
     if not args.no_extras:
         del mlp
         torch.cuda.empty_cache()
+        # the library bars first, on a GPU in the same state as the timed step
+        # (after the long LoRA stack the same GEMM read ~45 % slower)
+        libs = library_baselines(device, flush) if world == 1 else None
         xb = torch.randn(BLOCK_TOKENS, D, generator=g, device=device).to(torch.bfloat16)
         chains = {}
         for fused in ((False, True) if world > 1 else (False,)):
@@ -827,7 +830,6 @@ def run_ours(args) -> int:
         reductions = reduce_vs_nccl(ctx, world, rank, device, flush)
         sweep = skinny_sweep(world, device, flush)
         ulysses = ulysses_send(device, flush) if world == 1 else None
-        libs = library_baselines(device, flush) if world == 1 else None
         extras = {"ms_per_768p_block_linear_chain": block_ms,
                   "block_768p_tops": block_ops / (block_ms * 1e-3) / 1e12,
                   "block_768p_chain_ms": chains,

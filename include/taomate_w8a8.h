@@ -198,6 +198,19 @@ int tm_scaled_mm_i8_lora(void* out, int out_dtype, const int8_t* a, const int8_t
                          uint32_t epilogue, void* stream);
 
 /*
+ * LoRA down-projection t = x a^T (the inner linear of the reference's LoRA
+ * forward, src/taomate_hd/inference/lora_checkpoint.py:135-136 and 146-147,
+ * torch.nn.functional.linear(inputs, lora_a)): x bf16 [m, k] (row stride
+ * ldx), a bf16 [rank, k] (row stride lda), t bf16 [m, rank] (row stride ldt);
+ * rank in {8, 16, ..., 64}.  fp32 accumulation on the tensor cores, one
+ * rounding to bf16.  The three pointers 16-byte aligned and the three row
+ * strides multiples of 8 elements.  m == 0 is a no-op.  Feeds lora_t of
+ * tm_scaled_mm_i8_lora.
+ */
+int tm_lora_down_proj(void* t, int64_t ldt, const void* x, int64_t ldx, const void* a,
+                      int64_t lda, int rank, int64_t m, int64_t k, void* stream);
+
+/*
  * Merged QKV projection written straight into the Ulysses all-to-all send
  * layout (the reference's merged_qkv_sequence_to_heads builds it with a
  * permute copy, src/taomate_hd/distributed/ulysses.py:153-212): the GEMM of

@@ -28,7 +28,7 @@ CAPI_SO = LIB / "libtaomate_w8a8.so"
 TORCH_SO = LIB / "libtaomate_w8a8_torch.so"
 STAMP = LIB / "build.stamp"
 
-CUDA_SOURCES = ("runtime.cu", "quant.cu", "gemm_i8.cu", "peer_memory.cu")
+CUDA_SOURCES = ("runtime.cu", "quant.cu", "gemm_i8.cu", "peer_memory.cu", "lora_down.cu")
 TORCH_SOURCES = ("torch_ops.cpp",)
 ARCH_FLAGS = ("-gencode", "arch=compute_100a,code=sm_100a")
 NVCC_FLAGS = (*ARCH_FLAGS, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-shared")

@@ -270,6 +270,30 @@ void scaled_mm_i8_lora(at::Tensor& out, const at::Tensor& a, const at::Tensor& b
                "scaled_mm_i8_lora");
 }
 
+// LoRA down-projection t = x a^T (tm_lora_down_proj): x bf16 [m, k],
+// a bf16 [r, k], t bf16 [m, r]; rows contiguous, any row strides.
+void lora_down_proj(at::Tensor& t, const at::Tensor& x, const at::Tensor& a) {
+  check_cuda(x, x, "x");
+  check_cuda(a, x, "a");
+  check_cuda(t, x, "t");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && a.scalar_type() == at::kBFloat16 &&
+                  t.scalar_type() == at::kBFloat16,
+              "x, a and t must be bfloat16");
+  TORCH_CHECK(x.dim() == 2 && a.dim() == 2 && t.dim() == 2, "x, a and t must be 2-D");
+  const int64_t m = x.size(0), k = x.size(1), r = a.size(0);
+  TORCH_CHECK(a.size(1) == k, "x and a inner dimensions differ: ", k, " vs ", a.size(1));
+  TORCH_CHECK(t.size(0) == m && t.size(1) == r, "t must be [", m, ", ", r, "]");
+  TORCH_CHECK(x.stride(1) == 1 && a.stride(1) == 1 && t.stride(1) == 1,
+              "x, a and t must be row-major");
+  const int64_t ldx = m > 1 ? x.stride(0) : k;
+  const int64_t lda = r > 1 ? a.stride(0) : k;
+  const int64_t ldt = m > 1 ? t.stride(0) : r;
+  const c10::cuda::CUDAGuard guard(x.device());
+  check_status(tm_lora_down_proj(t.data_ptr(), ldt, x.data_ptr(), ldx, a.data_ptr(), lda,
+                                 static_cast<int>(r), m, k, stream_of(x)),
+               "lora_down_proj");
+}
+
 // Merged QKV projection into the Ulysses all-to-all send buffer
 // send [world, 3, m, ceil(heads / world) * head_dim] (tm_scaled_mm_i8_ulysses_send;
 // padded head slots are zeroed).
@@ -469,6 +493,7 @@ TORCH_LIBRARY(taomate_w8a8, m) {
       "scaled_mm_i8_ulysses_send(Tensor(a!) send, Tensor a, Tensor b, Tensor a_scales, "
       "Tensor b_scales, Tensor? bias, int num_heads, int head_dim, int world) -> ()");
   m.def("quantize_weight_int8(Tensor(a!) q, Tensor(b!) scales, Tensor w) -> ()");
+  m.def("lora_down_proj(Tensor(a!) t, Tensor x, Tensor a) -> ()");
   m.def(
       "modulate_int8_quant(Tensor(a!) out, Tensor(b!) scales, Tensor(c!)? hidden_out, Tensor x, "
       "Tensor shift, Tensor scale, Tensor? index) -> ()");
@@ -489,6 +514,7 @@ TORCH_LIBRARY_IMPL(taomate_w8a8, CUDA, m) {
   m.impl("scaled_mm_i8_lora", &scaled_mm_i8_lora);
   m.impl("scaled_mm_i8_ulysses_send", &scaled_mm_i8_ulysses_send);
   m.impl("quantize_weight_int8", &quantize_weight_int8);
+  m.impl("lora_down_proj", &lora_down_proj);
   m.impl("modulate_int8_quant", &modulate_int8_quant);
   m.impl("rms_norm_modulate_int8_quant", &rms_norm_modulate_int8_quant);
   m.impl("residual_gate_rms_norm_modulate_int8_quant",

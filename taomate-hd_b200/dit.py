@@ -323,8 +323,9 @@ class TPW8A8LoRABlockStack:
     the quant -> fc1 (+bias, LoRA, GELU-tanh) -> quant -> fc2 (+bias, LoRA)
     and its row reduction.  Every W8A8 linear adds its BF16 LoRA delta
     (rank 64, alpha 64) in the GEMM epilogue; the LoRA down-projection
-    T = x A^T is a plain bf16 GEMM.  Row-parallel linears follow the
-    reference's fused-row-reduce LoRA (lora_checkpoint.py:127-143):
+    T = x A^T is this package's tcgen05 bf16 kernel (``lora_down_proj``).
+    Row-parallel linears follow the reference's fused-row-reduce LoRA
+    (lora_checkpoint.py:127-143):
     reduce(partial + update) + bias, with the bias on TP rank 0 and an NCCL
     all-reduce.  Each block has its own random weights; activation buffers
     are shared by all blocks, so a forward allocates nothing.
@@ -381,12 +382,12 @@ class TPW8A8LoRABlockStack:
         return 2 * m * r * ((d + 3 * w) + (w + d) + (d + f) + (f + d))
 
     # this package's kernel launches per block: 2 modulate-quant + 2 quant + 4
-    # LoRA GEMMs (plus 4 bf16 LoRA down-projections on cuBLAS)
-    launches_per_block = 8
+    # LoRA down-projections + 4 LoRA GEMMs
+    launches_per_block = 12
 
     def _lora_linear(self, q: _Quant, w: W8Weight, lora: LoRAShard, x: torch.Tensor,
                      out: torch.Tensor, bias: torch.Tensor | None, gelu: bool = False) -> None:
-        torch.mm(x, lora.a.t(), out=self.t_buf)
+        torch.ops.taomate_w8a8.lora_down_proj(self.t_buf, x, lora.a)
         torch.ops.taomate_w8a8.scaled_mm_i8_lora(out, q.q, w.q_t, q.s, w.scale, bias, self.t_buf,
                                                  lora.b, ops.EPI_GELU_TANH if gelu else 0)
 

@@ -167,6 +167,22 @@ def scaled_mm_lora(
     return out
 
 
+def lora_down_proj(x: torch.Tensor, a: torch.Tensor, *,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    """LoRA down-projection ``x @ a.T`` in bf16 (the inner linear of the
+    reference's LoRA forward, lora_checkpoint.py:135-136 and 146-147): ``x``
+    bf16 ``[..., K]``, ``a`` bf16 ``[r, K]`` with r in {8, 16, ..., 64};
+    returns bf16 ``[M, r]`` (fp32 accumulation, one rounding), the
+    ``lora_t`` operand of :func:`scaled_mm_lora`.  Row strides must be
+    multiples of 8 elements."""
+    _require_cuda(x, a, out)
+    x2 = x.reshape(-1, x.shape[-1])
+    if out is None:
+        out = torch.empty((x2.shape[0], a.shape[0]), dtype=torch.bfloat16, device=x.device)
+    _ops.lora_down_proj(out, x2, a)
+    return out
+
+
 def quantize_weight_int8(weight: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """Per-output-channel symmetric int8 weight conversion on the GPU.
 

@@ -129,3 +129,61 @@ def test_lora_through_c_abi_and_errors(capi, cuda):
     assert call(ldt=68, ldlb=64, rank=64) == 3   # row stride not a multiple of 8
     assert call(t_ptr=t.data_ptr() + 8) == 3     # misaligned T
     assert np.isfinite(out.cpu().float().numpy()).all()
+
+
+@pytest.mark.parametrize("m,k,r,strided", [
+    (1, 64, 64, False),
+    (300, 1000, 8, False),      # K not a multiple of the 64-column k-block, smallest rank
+    (257, 512, 24, True),       # rank between MMA widths; x a column slice of a wider tensor
+    (1024, 3072, 48, False),
+    (2048, 3072, 64, True),     # the 768p down-projection shape (x = QKV output's Q part)
+    (640, 12288, 64, False),    # fc2's K
+])
+def test_down_projection_matches_fp32_reference(tm_ops, cuda, m, k, r, strided):
+    """T = x A^T (lora_checkpoint.py:135-136, 146-147) on the tensor cores
+    against a float64 product of the same bf16 operands: one bf16 rounding
+    (2^-8 relative) plus an allowance of 2^-16 of sum |x_i a_i| for the
+    order of the fp32 additions."""
+    g = torch.Generator().manual_seed(m + k + r)
+    width = k + 256 if strided else k
+    x_full = torch.randn(m, width, generator=g).to(torch.bfloat16)
+    x_full[:, 5] *= 20  # an outlier channel, as the DiT activations have
+    x = x_full[:, 64:64 + k] if strided else x_full
+    a = (torch.randn(r, k, generator=g) * 0.02).to(torch.bfloat16)
+    got = tm_ops.lora_down_proj(x.to(cuda) if not strided else x_full.to(cuda)[:, 64:64 + k],
+                                a.to(cuda)).cpu()
+    assert got.shape == (m, r) and got.dtype == torch.bfloat16
+    want = x.double() @ a.double().t()
+    mag = x.double().abs() @ a.double().abs().t()
+    bound = 2.0 ** -8 * want.abs() + 2.0 ** -16 * mag + 1e-30
+    excess = ((got.double() - want).abs() / bound).max().item()
+    assert excess <= 1.0, excess
+
+
+def test_down_projection_through_c_abi_feeds_the_lora_gemm(tm_ops, capi, cuda):
+    """The C-ABI call writes T into a strided buffer; the LoRA GEMM fed with
+    it matches the oracle composition; calls twice in a row give the same
+    bits."""
+    m, n, k, r = 384, 512, 768, 64
+    x, wq, ws, q, s, a_lora, b_lora, _ = _case(m, n, k, r, seed=21, b_std=0.05)
+    xb = x.to(torch.bfloat16).to(cuda)
+    al = a_lora.to(cuda)
+    t_buf = torch.full((m, r + 16), float("nan"), dtype=torch.bfloat16, device=cuda)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    rc = capi.tm_lora_down_proj(t_buf.data_ptr(), r + 16, xb.data_ptr(), k, al.data_ptr(), k, r,
+                                m, k, stream)
+    assert rc == 0
+    first = t_buf.clone()
+    assert capi.tm_lora_down_proj(t_buf.data_ptr(), r + 16, xb.data_ptr(), k, al.data_ptr(), k, r,
+                                  m, k, stream) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(first.view(torch.int16), t_buf.view(torch.int16))
+    assert torch.isnan(t_buf[:, r:].float()).all()  # columns past the rank untouched
+    t = t_buf[:, :r]
+    qd, wqd, sd, wsd = (torch.from_numpy(v).to(cuda) for v in (q, wq, s, ws))
+    out = tm_ops.scaled_mm_lora(qd, wqd.t(), sd.reshape(-1, 1), wsd.reshape(1, -1), t,
+                                b_lora.to(cuda))
+    base, _ = orc.scaled_mm(q, wq, s, ws, None, torch.bfloat16)
+    ref = orc.lora_column(base, x, a_lora, b_lora, 1.0)
+    torch.testing.assert_close(out.cpu().float(), ref.float(), atol=ATOL, rtol=RTOL)
+

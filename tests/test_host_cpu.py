@@ -189,6 +189,16 @@ def test_c_abi_host_argument_checks():
     assert args  # sizes used above
     tile = lib.tm_scaled_mm_i8_tile
     assert tile(p, 0, p, p, p, 128, p, 256, None, 128, 256, 512, 512, 512, 256, 0, None, 96, None) == capi_mod.TM_ERR_UNSUPPORTED
+    down = lib.tm_lora_down_proj  # (t, ldt, x, ldx, a, lda, rank, m, k, stream)
+    assert down(p, 64, p, 512, p, 512, 64, 0, 512, None) == capi_mod.TM_OK            # no rows
+    assert down(p, 72, p, 512, p, 512, 72, 128, 512, None) == capi_mod.TM_ERR_UNSUPPORTED
+    assert down(p, 64, p, 512, p, 512, 12, 128, 512, None) == capi_mod.TM_ERR_UNSUPPORTED
+    assert down(p, 32, p, 512, p, 512, 64, 128, 512, None) == capi_mod.TM_ERR_SHAPE  # ldt < rank
+    assert down(p, 64, p, 500, p, 512, 64, 128, 512, None) == capi_mod.TM_ERR_SHAPE  # ldx < k
+    assert down(p, 64, p, 516, p, 512, 64, 128, 512, None) == capi_mod.TM_ERR_ALIGNMENT
+    assert down(ctypes.c_void_p((1 << 20) + 8), 64, p, 512, p, 512, 64, 128, 512,
+                None) == capi_mod.TM_ERR_ALIGNMENT
+    assert down(None, 64, p, 512, p, 512, 64, 128, 512, None) == capi_mod.TM_ERR_NULL_POINTER
 
 
 def test_torch_ops_have_no_cpu_path():
