@@ -20,7 +20,9 @@ small shape and at the BASELINE shapes (480p fc2: 8192 x 3072 x 12288 / t;
   cancel its result can be far from the exact sum in relative terms; the
   check is the rounding bound itself: at most world + 2 roundings, each off
   by at most 2^-8 (bf16's unit roundoff) of the magnitudes involved, i.e.
-  |fused - nccl| <= (world + 2) * 2^-8 * (sum over ranks of |partial| + |fused|).
+  |fused - nccl| <= (world + 2) * 2^-8 * (sum of |partial| + |bias| + |fused|).
+  |bias| is there because the fused path rounds rank 0's partial before the
+  bias is added and NCCL's input after, and the two can nearly cancel.
 
 The ranks run as child processes with NCCL's NVLS off; each world size is
 skipped on a box with fewer GPUs.
@@ -142,7 +144,8 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
                     exact = bool(torch.equal(got.view(torch.int16), ref.view(torch.int16)))
                     err = float((got.float() - ref.float()).abs().max())
                     yf = y.float()
-                    bound = (world + 2) * 2.0 ** -8 * (mag_sum + yf.abs())
+                    bound = (world + 2) * 2.0 ** -8 * (mag_sum + bias.to(device).float().abs()
+                                                       + yf.abs())
                     excess = (yf - nccl.float()).abs() / bound.clamp_min(1e-30)
                     nccl_close = bool((excess <= 1.0).all())
                     nccl_excess = float(excess.max())
