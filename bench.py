@@ -296,36 +296,51 @@ def lora_block_stack(ctx, device: torch.device, g: torch.Generator, world: int,
     the BF16 LoRA (rank 64, alpha 64) in the W8A8 epilogue and adaLN modulate
     fused into the activation quant; each block has its own weights, so every
     block streams its weights from HBM.  One forward of the 40 blocks per
-    timed repetition (L2 flushed before it)."""
+    timed repetition (L2 flushed before it).  At N > 1 the row-parallel
+    out-projection and fc2 reductions run both ways, NCCL all-reduce and fused
+    into the LoRA GEMM over NVLink; the line's ms_per_block is the faster."""
     from taomate_hd_b200.dit import TPW8A8LoRABlockStack
 
-    stack = TPW8A8LoRABlockStack(STACK_BLOCKS, BLOCK_TOKENS, D, HEADS, HEAD_DIM, FFN, ctx, device,
-                                 seed=11)
     x = torch.randn(BLOCK_TOKENS, D, generator=g, device=device).to(torch.bfloat16)
-    stack.forward(x)
-    torch.cuda.synchronize()
-    barrier(world)
-    reps = 3
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(reps)]
-    for e0, e1 in ev:
-        flush.zero_()
-        e0.record()
+    per_mode = {}
+    for fused in ((False, True) if world > 1 else (False,)):
+        stack = TPW8A8LoRABlockStack(STACK_BLOCKS, BLOCK_TOKENS, D, HEADS, HEAD_DIM, FFN, ctx,
+                                     device, seed=11, fused=fused)
         stack.forward(x)
-        e1.record()
-    torch.cuda.synchronize()
-    barrier(world)
-    ms = max_over_ranks(sum(e0.elapsed_time(e1) for e0, e1 in ev) / reps, world, device)
-    per_block = ms / STACK_BLOCKS
-    out = {"blocks": STACK_BLOCKS, "ms_per_forward": ms, "ms_per_block": per_block,
-           "int8_tops": stack.int8_ops_per_block / (per_block * 1e-3) / 1e12,
-           "lora_bf16_tflops": stack.lora_flops_per_block / (per_block * 1e-3) / 1e12,
+        torch.cuda.synchronize()
+        barrier(world)
+        reps = 3
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(reps)]
+        for e0, e1 in ev:
+            flush.zero_()
+            e0.record()
+            stack.forward(x)
+            e1.record()
+        torch.cuda.synchronize()
+        barrier(world)
+        ms = max_over_ranks(sum(e0.elapsed_time(e1) for e0, e1 in ev) / reps, world, device)
+        per_mode["fused" if fused else "nccl"] = ms / STACK_BLOCKS
+        if fused:
+            stack.close()
+            barrier(world)
+        ops_per_block, lora_flops, launches = (stack.int8_ops_per_block,
+                                               stack.lora_flops_per_block,
+                                               stack.launches_per_block)
+        del stack
+        torch.cuda.empty_cache()
+    per_block = min(per_mode.values())
+    out = {"blocks": STACK_BLOCKS, "ms_per_forward": per_block * STACK_BLOCKS,
+           "ms_per_block": per_block, "ms_per_block_by_reduce": per_mode,
+           "int8_tops": ops_per_block / (per_block * 1e-3) / 1e12,
+           "lora_bf16_tflops": lora_flops / (per_block * 1e-3) / 1e12,
            "config": f"M={BLOCK_TOKENS}, d={D}, heads {HEADS}x{HEAD_DIM}, ffn {FFN}, LoRA rank "
-                     f"{stack.rank} alpha 64 in every W8A8 epilogue, per-token adaLN modulate fused "
-                     "into the quant, GELU-tanh after fc1; row-parallel reduce: "
-                     + ("none (TP=1)" if world == 1 else "NCCL all-reduce"),
-           "gpu_launches_per_block": stack.launches_per_block}
-    del stack
+                     "64 alpha 64 in every W8A8 epilogue (down-projection on this package's "
+                     "tcgen05 kernel), per-token adaLN modulate fused into the quant, GELU-tanh "
+                     "after fc1; row-parallel reduce: "
+                     + ("none (TP=1)" if world == 1
+                        else "NCCL all-reduce or fused into the LoRA GEMM (the faster)"),
+           "gpu_launches_per_block": launches}
     return out
 
 

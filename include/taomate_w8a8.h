@@ -198,6 +198,37 @@ int tm_scaled_mm_i8_lora(void* out, int out_dtype, const int8_t* a, const int8_t
                          uint32_t epilogue, void* stream);
 
 /*
+ * The row-parallel LoRA linears with their reduction fused into the kernel
+ * (the reference's fused-row-reduce LoRA forward,
+ * src/taomate_hd/inference/lora_checkpoint.py:127-143: each rank adds its
+ * update_partial * scale to base_partial, the sum is reduced over the TP
+ * group, then the bias is added): the LoRA epilogue of tm_scaled_mm_i8_lora
+ * with no activation, whose bf16 partial goes to the rows' owners as in
+ * tm_scaled_mm_i8_reduce_scatter / tm_scaled_mm_i8_all_reduce (same peer
+ * buffers, counters, epochs and rules).  Each rank's partial is
+ * round(round(dequant(a b^T)) + lora_t lora_b^T) (fp32 add, one rounding);
+ * the owner sums the partials in rank order in fp32, adds the bias once and
+ * rounds.  bf16 output only.
+ */
+int tm_scaled_mm_i8_lora_reduce_scatter(void* out, const int8_t* a, const int8_t* b,
+                                        const float* scale_a, int64_t scale_a_numel,
+                                        const float* scale_b, int64_t scale_b_numel,
+                                        const void* bias, const void* lora_t, int64_t ldt,
+                                        const void* lora_b, int64_t ldlb, int lora_rank,
+                                        int64_t m, int64_t n, int64_t k, int64_t lda,
+                                        int64_t ldb, int64_t ldo, void* const* peer_part,
+                                        void* const* peer_flags, int world, int rank,
+                                        uint32_t epoch, void* stream);
+int tm_scaled_mm_i8_lora_all_reduce(const int8_t* a, const int8_t* b, const float* scale_a,
+                                    int64_t scale_a_numel, const float* scale_b,
+                                    int64_t scale_b_numel, const void* bias, const void* lora_t,
+                                    int64_t ldt, const void* lora_b, int64_t ldlb, int lora_rank,
+                                    int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
+                                    void* const* peer_part, void* const* peer_flags,
+                                    void* const* peer_out, int world, int rank, uint32_t epoch,
+                                    void* stream);
+
+/*
  * LoRA down-projection t = x a^T (the inner linear of the reference's LoRA
  * forward, src/taomate_hd/inference/lora_checkpoint.py:135-136 and 146-147,
  * torch.nn.functional.linear(inputs, lora_a)): x bf16 [m, k] (row stride

@@ -62,6 +62,14 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         c_int, [*_GEMM, c_u32, c_void_p, c_int, c_int, c_void_p, ctypes.c_uint64, c_void_p]),
     "tm_scaled_mm_i8_splitk_workspace_size": (
         c_int, [c_i64, c_i64, c_i64, c_int, c_int, ctypes.POINTER(ctypes.c_uint64)]),
+    "tm_scaled_mm_i8_lora_reduce_scatter": (
+        c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_void_p, c_i64, c_void_p,
+                c_void_p, c_i64, c_void_p, c_i64, c_int, c_i64, c_i64, c_i64, c_i64, c_i64,
+                c_i64, c_void_p, c_void_p, c_int, c_int, c_u32, c_void_p]),
+    "tm_scaled_mm_i8_lora_all_reduce": (
+        c_int, [c_void_p, c_void_p, c_void_p, c_i64, c_void_p, c_i64, c_void_p,
+                c_void_p, c_i64, c_void_p, c_i64, c_int, c_i64, c_i64, c_i64, c_i64, c_i64,
+                c_void_p, c_void_p, c_void_p, c_int, c_int, c_u32, c_void_p]),
     "tm_lora_down_proj": (
         c_int, [c_void_p, c_i64, c_void_p, c_i64, c_void_p, c_i64, c_int, c_i64, c_i64, c_void_p]),
     "tm_scaled_mm_i8_lora": (

@@ -1579,6 +1579,37 @@ __device__ __forceinline__ void lora_store_tile(const GemmArgs& g, const CUtenso
   }
 }
 
+// Phase 3 for scatter outputs (the row-parallel reduce-scatter / all-reduce
+// modes, which allow no activation): read y + T B^T, round, and store each
+// 64-column half through the row-per-lane staging tile as 128-byte row
+// segments to the rows' owners (out_row_ptr), like epilogue_tile.  The
+// column cache in the same region is dead by now (phase 1 used it).
+template <typename OutT, typename Release>
+__device__ __forceinline__ void lora_store_tile_scatter(const GemmArgs& g, uint32_t t_row,
+                                                        int64_t row_base, int col_base, int lane,
+                                                        uint8_t* region, Release release) {
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c * 32), r);
+    tmem_ld_wait();
+    if (c == 3) release();
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      *stage_slot(region, lane, (c & 1) * 4 + q) = make_uint4(
+          pack2<OutT>(__uint_as_float(r[8 * q]), __uint_as_float(r[8 * q + 1])),
+          pack2<OutT>(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3])),
+          pack2<OutT>(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5])),
+          pack2<OutT>(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7])));
+    if (c & 1) {
+      __syncwarp();
+      write_staged<OutT>(g, region, row_base, col_base + (c - 1) * 32,
+                         64 * static_cast<int>(sizeof(OutT)) / 16, lane);
+      __syncwarp();
+    }
+  }
+}
+
 template <int STAGES, typename OutT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_i8_pair_lora_kernel(const __grid_constant__ CUtensorMap tm_a,
@@ -1805,6 +1836,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                      map_to_cta(smem_u32(&conv[1]), 0)};
     int acc = 0;
     uint32_t acc_phase = 0;
+    long long sent[kMaxPeers] = {};
     uint8_t* region = smem + L::kEpiOffset + (warp - 2) * kEpiStageBytes;
     const int q = warp & 3;
     const int h = (warp - 2) >> 2;
@@ -1844,14 +1876,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(empty_leader[acc]);
       };
-      lora_store_tile<OutT>(g, &tm_out, t_row, row_base, nb * BN + h * kBNHalf, lane, region,
-                            release);
+      if (g.tma_store)
+        lora_store_tile<OutT>(g, &tm_out, t_row, row_base, nb * BN + h * kBNHalf, lane, region,
+                              release);
+      else
+        lora_store_tile_scatter<OutT>(g, t_row, row_base, nb * BN + h * kBNHalf, lane, region,
+                                      release);
+      const int64_t tile_row0 = static_cast<int64_t>(mb) * 2 * kBM + rank * kBM;
+      if (g.world > 0 && tile_row0 < g.M)
+        sent[static_cast<int>(tile_row0 / g.rows_per_owner)] += kBM * min(BN, g.N - nb * BN);
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
       }
     }
-    if (lane == 0) bulk_wait_all();
+    if (g.tma_store && lane == 0) bulk_wait_all();
+    if (g.world > 0) publish_counts(g, sent, warp, lane);
   }
 
   tc_fence_before();
@@ -1860,6 +1900,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, 512);
   }
+  if (g.world > 0) reduce_phase(g, BN, blockIdx.x, gridDim.x);
 }
 
 // ====================================================================== host
@@ -2006,20 +2047,24 @@ int launch_pair_lora(const Operands& op, GemmArgs args, const LoraSpec& lora, in
   using L = LoraSmem<kStages>;
   args.num_m = (args.M + 2 * kBM - 1) / (2 * kBM);
   args.num_n = (args.N + 255) / 256;
+  args.m_owners = args.world;
+  args.mb_per_owner = args.world > 0 ? args.rows_per_owner / (2 * kBM) : 0;
   args.group_n = choose_group_n(args.num_n, 2 * kBM, 256, args.K);
-  args.tma_store = 1;
+  args.tma_store = args.world == 0;  // scatter outputs go to peers as row segments
   const CUtensorMapDataType dt = std::is_same<OutT, __nv_bfloat16>::value
                                      ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap ta, tb, to, tlt, tlb;
+  memset(&to, 0, sizeof(to));  // never read without the TMA-store epilogue
   // T and B_lora: r columns, boxes of 64 columns (128 bytes; columns past r
   // read as zero) x 128 rows
   if (!encode_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, op.a, args.K, args.M, op.lda, kBK, kBM,
                       CU_TENSOR_MAP_SWIZZLE_128B) ||
       !encode_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, op.b, args.K, args.N, op.ldb, kBK, 128,
                       CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_tmap_2d(&to, dt, args.out, args.N, args.M, static_cast<uint64_t>(args.ldo) * 2, 32,
-                      32, CU_TENSOR_MAP_SWIZZLE_64B) ||
+      (args.tma_store &&
+       !encode_tmap_2d(&to, dt, args.out, args.N, args.M, static_cast<uint64_t>(args.ldo) * 2,
+                       32, 32, CU_TENSOR_MAP_SWIZZLE_64B)) ||
       !encode_tmap_2d(&tlt, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, lora.t, lora.rank, args.M,
                       static_cast<uint64_t>(lora.ldt) * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !encode_tmap_2d(&tlb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, lora.b, lora.rank, args.N,
@@ -2036,13 +2081,21 @@ int launch_pair_lora(const Operands& op, GemmArgs args, const LoraSpec& lora, in
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = L::kTotal;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  if (launch_with_pdl(cfg, attr, 1, kernel, ta, tb, to, tlt, tlb, args) != cudaSuccess)
-    return TM_ERR_CUDA;
+  // The fused reduction waits on blocks produced by other CTAs of the same
+  // launch: require them all to be resident at once.
+  attr[1].id = cudaLaunchAttributeCooperative;
+  attr[1].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const cudaError_t err = args.world > 0
+                              ? cudaLaunchKernelEx(&cfg, kernel, ta, tb, to, tlt, tlb, args)
+                              : launch_with_pdl(cfg, attr, 1, kernel, ta, tb, to, tlt, tlb, args);
+  if (err != cudaSuccess) return TM_ERR_CUDA;
   return check_launch();
 }
 
@@ -2382,6 +2435,17 @@ int scaled_mm_impl(void* out, int out_dtype, const int8_t* a, const int8_t* b, c
 // a pointer (on the host it is only a stand-in for the symbol); its device
 // address is looked up once per device with cudaGetSymbolAddress while that
 // device is current.
+// Host checks of the LoRA operands shared by the LoRA entry points.
+int check_lora(const void* lora_t, int64_t ldt, const void* lora_b, int64_t ldlb, int lora_rank,
+               int64_t m) {
+  if (lora_rank < 8 || lora_rank > 64 || lora_rank % 8 != 0) return TM_ERR_UNSUPPORTED;
+  if (ldt < lora_rank || ldlb < lora_rank) return TM_ERR_SHAPE;
+  if (ldt % 8 != 0 || ldlb % 8 != 0) return TM_ERR_ALIGNMENT;
+  if (m > 0 && (lora_t == nullptr || lora_b == nullptr)) return TM_ERR_NULL_POINTER;
+  if ((lora_t && !aligned16(lora_t)) || (lora_b && !aligned16(lora_b))) return TM_ERR_ALIGNMENT;
+  return TM_OK;
+}
+
 constexpr uint64_t kNoAllocScratchBytes = TM_SPLITK_NOALLOC_MAX_BYTES;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
@@ -2499,16 +2563,52 @@ int tm_scaled_mm_i8_lora(void* out, int out_dtype, const int8_t* a, const int8_t
                          int64_t ldt, const void* lora_b, int64_t ldlb, int lora_rank, int64_t m,
                          int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldo,
                          uint32_t epilogue, void* stream) {
-  if (lora_rank < 8 || lora_rank > 64 || lora_rank % 8 != 0) return TM_ERR_UNSUPPORTED;
-  if (ldt < lora_rank || ldlb < lora_rank) return TM_ERR_SHAPE;
-  if (ldt % 8 != 0 || ldlb % 8 != 0) return TM_ERR_ALIGNMENT;
-  if (m > 0 && (lora_t == nullptr || lora_b == nullptr)) return TM_ERR_NULL_POINTER;
-  if ((lora_t && !tmw::aligned16(lora_t)) || (lora_b && !tmw::aligned16(lora_b)))
-    return TM_ERR_ALIGNMENT;
+  const int rc = tmw::check_lora(lora_t, ldt, lora_b, ldlb, lora_rank, m);
+  if (rc != TM_OK) return rc;
   const tmw::LoraSpec spec{lora_t, ldt, lora_b, ldlb, lora_rank};
   return tmw::scaled_mm_impl(out, out_dtype, a, b, scale_a, scale_a_numel, scale_b, scale_b_numel,
                              bias, m, n, k, lda, ldb, ldo, epilogue, nullptr, 0,
                              tmw::as_stream(stream), nullptr, nullptr, &spec);
+}
+
+int tm_scaled_mm_i8_lora_reduce_scatter(void* out, const int8_t* a, const int8_t* b,
+                                        const float* scale_a, int64_t scale_a_numel,
+                                        const float* scale_b, int64_t scale_b_numel,
+                                        const void* bias, const void* lora_t, int64_t ldt,
+                                        const void* lora_b, int64_t ldlb, int lora_rank,
+                                        int64_t m, int64_t n, int64_t k, int64_t lda,
+                                        int64_t ldb, int64_t ldo, void* const* peer_part,
+                                        void* const* peer_flags, int world, int rank,
+                                        uint32_t epoch, void* stream) {
+  const int rc = tmw::check_lora(lora_t, ldt, lora_b, ldlb, lora_rank, m);
+  if (rc != TM_OK) return rc;
+  const tmw::LoraSpec lora{lora_t, ldt, lora_b, ldlb, lora_rank};
+  const tmw::ScatterSpec spec{peer_part, peer_flags, world, rank, epoch};
+  return tmw::scaled_mm_impl(out, TM_DTYPE_BF16, a, b, scale_a, scale_a_numel, scale_b,
+                             scale_b_numel, bias, m, n, k, lda, ldb, ldo, 0u, nullptr, 0,
+                             tmw::as_stream(stream), &spec, nullptr, &lora);
+}
+
+int tm_scaled_mm_i8_lora_all_reduce(const int8_t* a, const int8_t* b, const float* scale_a,
+                                    int64_t scale_a_numel, const float* scale_b,
+                                    int64_t scale_b_numel, const void* bias, const void* lora_t,
+                                    int64_t ldt, const void* lora_b, int64_t ldlb, int lora_rank,
+                                    int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
+                                    void* const* peer_part, void* const* peer_flags,
+                                    void* const* peer_out, int world, int rank, uint32_t epoch,
+                                    void* stream) {
+  const int rc = tmw::check_lora(lora_t, ldt, lora_b, ldlb, lora_rank, m);
+  if (rc != TM_OK) return rc;
+  if (peer_out == nullptr) return TM_ERR_NULL_POINTER;
+  if (world < 1 || world > tmw::kMaxPeers) return TM_ERR_TOO_LARGE;
+  if (rank < 0 || rank >= world) return TM_ERR_SHAPE;
+  if (peer_out[rank] == nullptr) return TM_ERR_NULL_POINTER;
+  const tmw::LoraSpec lora{lora_t, ldt, lora_b, ldlb, lora_rank};
+  const tmw::ScatterSpec spec{peer_part, peer_flags, world, rank, epoch, peer_out};
+  void* own_rows = static_cast<__nv_bfloat16*>(peer_out[rank]) + rank * (m / world) * n;
+  return tmw::scaled_mm_impl(own_rows, TM_DTYPE_BF16, a, b, scale_a, scale_a_numel, scale_b,
+                             scale_b_numel, bias, m, n, k, lda, ldb, n, 0u, nullptr, 0,
+                             tmw::as_stream(stream), &spec, nullptr, &lora);
 }
 
 int tm_scaled_mm_i8_ulysses_send(void* send, int out_dtype, const int8_t* a, const int8_t* b,

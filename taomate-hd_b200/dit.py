@@ -325,15 +325,18 @@ class TPW8A8LoRABlockStack:
     (rank 64, alpha 64) in the GEMM epilogue; the LoRA down-projection
     T = x A^T is this package's tcgen05 bf16 kernel (``lora_down_proj``).
     Row-parallel linears follow the reference's fused-row-reduce LoRA
-    (lora_checkpoint.py:127-143):
-    reduce(partial + update) + bias, with the bias on TP rank 0 and an NCCL
-    all-reduce.  Each block has its own random weights; activation buffers
-    are shared by all blocks, so a forward allocates nothing.
+    (lora_checkpoint.py:127-143): reduce(partial + update) + bias.  With
+    ``fused=True`` (TP > 1) that reduction runs inside the LoRA GEMM launch
+    over NVLink (``PeerAllReduce.lora``; one buffer pair serves the
+    out-projection and fc2, which have the same shape); otherwise the bias
+    goes on TP rank 0 and NCCL all-reduces.  Each block has its own random
+    weights; activation buffers are shared by all blocks, so a forward
+    allocates nothing.
     """
 
     def __init__(self, n_blocks: int, tokens: int, d: int, heads: int, head_dim: int, ffn: int,
                  ctx: ParallelContext, device: torch.device, *, rank: int = 64,
-                 alpha: float = 64.0, seed: int = 0):
+                 alpha: float = 64.0, seed: int = 0, fused: bool = False):
         t = ctx.tp_world_size
         width = heads * head_dim
         if heads % t or ffn % t:
@@ -368,6 +371,11 @@ class TPW8A8LoRABlockStack:
         self.h = torch.empty(tokens, ffn // t, **bf)
         self.q2 = _Quant(tokens, ffn // t, device)
         self.y = [torch.empty(tokens, d, **bf) for _ in range(2)]
+        self.peer_ar = None
+        if fused and t > 1:
+            from .peer_reduce import PeerAllReduce
+
+            self.peer_ar = PeerAllReduce(ctx, tokens, d, device)
 
     @property
     def int8_ops_per_block(self) -> int:
@@ -391,6 +399,22 @@ class TPW8A8LoRABlockStack:
         torch.ops.taomate_w8a8.scaled_mm_i8_lora(out, q.q, w.q_t, q.s, w.scale, bias, self.t_buf,
                                                  lora.b, ops.EPI_GELU_TANH if gelu else 0)
 
+    def _row_lora_linear(self, q: _Quant, w: W8Weight, lora: LoRAShard, x: torch.Tensor,
+                         out: torch.Tensor) -> torch.Tensor:
+        """Row-parallel LoRA linear and its reduction over the TP group."""
+        if self.peer_ar is not None:
+            torch.ops.taomate_w8a8.lora_down_proj(self.t_buf, x, lora.a)
+            return self.peer_ar.lora(q.q, q.s, w.q, w.scale, w.bias, self.t_buf, lora.b)
+        self._lora_linear(q, w, lora, x, out, w.bias if self.ctx.tp_rank == 0 else None)
+        return self._reduce(out)
+
+    def close(self) -> None:
+        """Release the fused reduction's peer buffers (collective: every rank)."""
+        if self.peer_ar is not None:
+            self.peer_ar.check()
+            self.peer_ar.close()
+            self.peer_ar = None
+
     def _reduce(self, y: torch.Tensor) -> torch.Tensor:
         t = self.ctx.tp_world_size
         if t == 1:
@@ -398,24 +422,18 @@ class TPW8A8LoRABlockStack:
         return all_reduce_sum_inplace_(y, group=self.ctx.tp_group, world_size=t)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        t, first = self.ctx.tp_world_size, self.ctx.tp_rank == 0
         for i, blk in enumerate(self.blocks):
             torch.ops.taomate_w8a8.modulate_int8_quant(self.q_in.q, self.q_in.s, self.hidden, x,
                                                        self.shift1, self.scale1, None)
             self._lora_linear(self.q_in, blk.qkv, blk.qkv_lora, self.hidden, self.qkv_out,
                               blk.qkv.bias)
-            attn = self.qkv_out[:, : self.width // t]
+            attn = self.qkv_out[:, : self.width // self.ctx.tp_world_size]
             self.q_attn(attn)
-            self._lora_linear(self.q_attn, blk.out, blk.out_lora, attn, self.attn_out,
-                              blk.out.bias if first else None)
-            a = self._reduce(self.attn_out)
+            a = self._row_lora_linear(self.q_attn, blk.out, blk.out_lora, attn, self.attn_out)
             torch.ops.taomate_w8a8.modulate_int8_quant(self.q_in.q, self.q_in.s, self.hidden, a,
                                                        self.shift2, self.scale2, None)
             self._lora_linear(self.q_in, blk.fc1, blk.fc1_lora, self.hidden, self.h, blk.fc1.bias,
                               gelu=True)
             self.q2(self.h)
-            y = self.y[i % 2]
-            self._lora_linear(self.q2, blk.fc2, blk.fc2_lora, self.h, y,
-                              blk.fc2.bias if first else None)
-            x = self._reduce(y)
+            x = self._row_lora_linear(self.q2, blk.fc2, blk.fc2_lora, self.h, self.y[i % 2])
         return x

@@ -200,6 +200,31 @@ class PeerReduceScatter(_PeerBuffers):
         self._after_call()
         return out
 
+    def lora(self, q: torch.Tensor, q_scale: torch.Tensor, w_q: torch.Tensor,
+             w_scale: torch.Tensor, bias: torch.Tensor | None, lora_t: torch.Tensor,
+             lora_b: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """The row-parallel LoRA linear with its reduce-scatter fused
+        (lora_checkpoint.py:127-143, fused-row-reduce branch): each rank's
+        ``round(round(q @ w_q^T) + lora_t @ lora_b^T)`` partial goes to the row
+        owners, which sum in rank order and add ``bias`` once.  ``lora_t`` bf16
+        ``[rows, r]`` (this rank's ``x_local A_local^T``), ``lora_b`` bf16
+        ``[cols, r]`` carrying the adapter scale."""
+        m, k = self._check(q, w_q)
+        if out.shape != (self.rows_per_owner, self.cols) or out.dtype != torch.bfloat16:
+            raise ValueError(f"out must be bf16 [{self.rows_per_owner}, {self.cols}]")
+        r = lora_t.shape[1]
+        half, stream = self._next_set()
+        rc = self._lib.tm_scaled_mm_i8_lora_reduce_scatter(
+            out.data_ptr(), q.data_ptr(), w_q.data_ptr(), q_scale.data_ptr(), q_scale.numel(),
+            w_scale.data_ptr(), w_scale.numel(), None if bias is None else bias.data_ptr(),
+            lora_t.data_ptr(), lora_t.stride(0), lora_b.data_ptr(), lora_b.stride(0), r,
+            m, self.cols, k, q.stride(0), w_q.stride(0), out.stride(0),
+            self._part[half], self._counts[half], self.world, self.rank, self._uses[half], stream)
+        if rc != 0:
+            self._raise("tm_scaled_mm_i8_lora_reduce_scatter", rc)
+        self._after_call()
+        return out
+
 
 class PeerAllReduce(_PeerBuffers):
     """Symmetric buffers + the fused GEMM/all-reduce for one shape.
@@ -231,5 +256,26 @@ class PeerAllReduce(_PeerBuffers):
             self._outs[half], self.world, self.rank, self._uses[half], tile_n, stream)
         if rc != 0:
             self._raise("tm_scaled_mm_i8_all_reduce", rc)
+        self._after_call()
+        return self._views[half]
+
+    def lora(self, q: torch.Tensor, q_scale: torch.Tensor, w_q: torch.Tensor,
+             w_scale: torch.Tensor, bias: torch.Tensor | None, lora_t: torch.Tensor,
+             lora_b: torch.Tensor) -> torch.Tensor:
+        """The row-parallel LoRA linear with its all-reduce fused: as
+        :meth:`PeerReduceScatter.lora`, then every owner's reduced rows reach
+        every rank; returns ``[rows, cols]`` (valid until the second call
+        after this one)."""
+        m, k = self._check(q, w_q)
+        r = lora_t.shape[1]
+        half, stream = self._next_set()
+        rc = self._lib.tm_scaled_mm_i8_lora_all_reduce(
+            q.data_ptr(), w_q.data_ptr(), q_scale.data_ptr(), q_scale.numel(),
+            w_scale.data_ptr(), w_scale.numel(), None if bias is None else bias.data_ptr(),
+            lora_t.data_ptr(), lora_t.stride(0), lora_b.data_ptr(), lora_b.stride(0), r,
+            m, self.cols, k, q.stride(0), w_q.stride(0), self._part[half], self._counts[half],
+            self._outs[half], self.world, self.rank, self._uses[half], stream)
+        if rc != 0:
+            self._raise("tm_scaled_mm_i8_lora_all_reduce", rc)
         self._after_call()
         return self._views[half]

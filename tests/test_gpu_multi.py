@@ -1,5 +1,6 @@
 """GPU, 2 / 4 / 8 ranks on as many GPUs: the fused row-parallel reduce-scatter
-and all-reduce, plus the failure path of their bounded waits on one GPU.
+and all-reduce (plain and with the LoRA delta), plus the failure path of
+their bounded waits on one GPU.
 
 Each rank holds a K-shard of a row-parallel W8A8 linear (linear.py:259-289
 semantics: per-token activation scales and per-channel weight scales over the
@@ -157,6 +158,45 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
                     checks.append((mode, m, n, k, call, exact, err, nccl_close, nccl_excess, kept))
                 peer.check()
                 peer.close()
+        # Row-parallel LoRA linears with the fused reduction
+        # (lora_checkpoint.py:127-143): every rank's partial is the LoRA GEMM's
+        # own epilogue output (no bias); the owners sum them in rank order in
+        # fp32 and add the bias once, so the result equals the gathered
+        # partials summed that way, bit for bit.
+        m, n, kl, r_lora = 512 * world, 768, 256, 64
+        g = torch.Generator(device=device).manual_seed(70 + rank)
+        q = torch.randint(-127, 128, (m, kl), generator=g, device=device, dtype=torch.int8)
+        wq = torch.randint(-127, 128, (n, kl), generator=g, device=device, dtype=torch.int8)
+        sq = torch.rand(m, 1, generator=g, device=device) * 1e-2
+        sw = torch.rand(n, generator=g, device=device) * 1e-3
+        t_l = torch.randn(m, r_lora, generator=g, device=device).to(torch.bfloat16)
+        b_l = (torch.randn(n, r_lora, generator=g, device=device) * 0.02).to(torch.bfloat16)
+        bias = (torch.randn(n, generator=torch.Generator(device=device).manual_seed(71),
+                            device=device) * 0.01).to(torch.bfloat16)
+        partial = ops.scaled_mm_lora(q, wq.t(), sq, sw.reshape(1, -1), t_l, b_l)
+        parts = [torch.empty_like(partial) for _ in range(world)]
+        torch.distributed.all_gather(parts, partial, group=group)
+        acc = torch.zeros(m, n, dtype=torch.float32, device=device)
+        for part in parts:
+            acc += part.float()
+        want = (acc + bias.float()).to(torch.bfloat16)
+        rows = m // world
+        for mode in ("lora_ar", "lora_rs"):
+            peer = (PeerAllReduce if mode == "lora_ar" else PeerReduceScatter)(ctx, m, n, device)
+            out = torch.empty(rows, n, dtype=torch.bfloat16, device=device)
+            for call in range(2):
+                if mode == "lora_ar":
+                    y = peer.lora(q, sq, wq, sw, bias, t_l, b_l)
+                    ref = want
+                else:
+                    y = peer.lora(q, sq, wq, sw, bias, t_l, b_l, out)
+                    ref = want[rank * rows:(rank + 1) * rows]
+                torch.cuda.synchronize()
+                exact = bool(torch.equal(y.view(torch.int16), ref.view(torch.int16)))
+                err = float((y.float() - ref.float()).abs().max())
+                checks.append((mode, m, n, kl * world, call, exact, err, True, 0.0, True))
+            peer.check()
+            peer.close()
         # Ulysses exchange of a merged QKV projection: the fused send layout
         # through NCCL's all-to-all equals the reference path (permute the
         # ordinary output, then the same all-to-all)
