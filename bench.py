@@ -471,6 +471,40 @@ def ulysses_send(device: torch.device, flush: torch.Tensor) -> list[dict]:
     return rows
 
 
+def ulysses_exchange(ctx, world: int, device: torch.device, flush: torch.Tensor) -> dict:
+    """768p merged QKV projection and its Ulysses all-to-all at degree = N
+    (tokens / N rows per rank, all heads): the exchange done by the GEMM's
+    epilogue over NVLink (``PeerUlyssesExchange``) against the send-layout
+    GEMM followed by NCCL's ``all_to_all_single`` (both return the
+    reference's (q, k, v)); median us, L2 flushed, max over ranks."""
+    from taomate_hd_b200.ulysses import PeerUlyssesExchange, merged_qkv_sequence_to_heads_w8a8
+
+    g = torch.Generator(device=device).manual_seed(79)
+    n, m = 3 * HEADS * HEAD_DIM, BLOCK_TOKENS // world
+    w = torch.randint(-127, 128, (n, D), generator=g, device=device, dtype=torch.int8)
+    sw = torch.rand(n, generator=g, device=device) * 1e-3 + 1e-5
+    bias = (torch.randn(n, generator=g, device=device) * 0.01).to(torch.bfloat16)
+    a = torch.randint(-127, 128, (m, D), generator=g, device=device, dtype=torch.int8)
+    sa = torch.rand(m, 1, generator=g, device=device) * 1e-2 + 1e-4
+    ex = PeerUlyssesExchange(ctx, m, HEADS, HEAD_DIM, device)
+    group = ctx.tp_group
+    fused = _timed(lambda: ex(a, sa, w, sw, bias), 10, flush, world, device)
+    nccl = _timed(lambda: merged_qkv_sequence_to_heads_w8a8(
+        a, sa, w, sw, bias, num_heads=HEADS, head_dim=HEAD_DIM, group=group, world=world),
+        10, flush, world, device)
+    same = all(torch.equal(x.view(torch.int16), y.view(torch.int16)) for x, y in zip(
+        ex(a, sa, w, sw, bias), merged_qkv_sequence_to_heads_w8a8(
+            a, sa, w, sw, bias, num_heads=HEADS, head_dim=HEAD_DIM, group=group, world=world)))
+    ex.check()
+    barrier(world)
+    ex.close()
+    moved = (world - 1) / world * m * n * 2  # bytes each rank sends to its peers
+    return {"degree": world, "tokens_per_rank": m, "n": n, "k": D,
+            "fused_us": round(1e3 * fused, 1), "send_gemm_plus_nccl_us": round(1e3 * nccl, 1),
+            "bytes_leaving_rank": moved, "nvlink_gbs_fused": round(moved / (fused * 1e-3) / 1e9, 1),
+            "bit_identical": same}
+
+
 def _timed(fn, reps: int, flush: torch.Tensor, world: int, device) -> float:
     """Median device time (ms) of ``fn`` over ``reps`` calls, L2 flushed before
     each, barrier-separated, max over ranks."""
@@ -845,6 +879,7 @@ def run_ours(args) -> int:
         reductions = reduce_vs_nccl(ctx, world, rank, device, flush)
         sweep = skinny_sweep(world, device, flush)
         ulysses = ulysses_send(device, flush) if world == 1 else None
+        ulysses_x = ulysses_exchange(ctx, world, device, flush) if world > 1 else None
         extras = {"ms_per_768p_block_linear_chain": block_ms,
                   "block_768p_tops": block_ops / (block_ms * 1e-3) / 1e12,
                   "block_768p_chain_ms": chains,
@@ -856,6 +891,7 @@ def run_ours(args) -> int:
                   "reduce_vs_nccl": reductions,
                   "skinny_sweep": sweep,
                   "ulysses_send_768p": ulysses,
+                  "ulysses_exchange_768p": ulysses_x,
                   "library_baselines": libs}
 
     if rank == 0:

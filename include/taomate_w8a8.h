@@ -198,6 +198,34 @@ int tm_scaled_mm_i8_lora(void* out, int out_dtype, const int8_t* a, const int8_t
                          uint32_t epilogue, void* stream);
 
 /*
+ * The merged QKV projection with the Ulysses all-to-all done by its epilogue
+ * over NVLink (the reference's merged_qkv_sequence_to_heads,
+ * src/taomate_hd/distributed/ulysses.py:166-212: the linear, the send
+ * layout, then all_to_all_single): each 64-column pass of the output is
+ * stored straight into the receive buffer of the rank that holds its head,
+ * in this rank's slot, so that every rank's peer_recv[j] ends up as the
+ * reference's all-to-all output [world][3][m][ceil(heads / world)][head_dim]
+ * (slot s from rank s; padded head slots are never written and stay as the
+ * buffer was zeroed at allocation).  Each CTA drains its stores once and
+ * adds its per-destination element counts to peer_flags[w][rank]; the launch
+ * returns when this rank's `world` counters show every source's rows
+ * (epoch x 3 x m x its real heads x head_dim), so the buffer is complete for
+ * the work that follows on `stream`.  peer_recv[j] / peer_flags[j]: rank j's
+ * receive buffer and `world` uint64 counters (zeroed at allocation, never
+ * reset; alternate two buffer sets by call, epoch = uses of the set).  m
+ * tokens per rank (m % 32 == 0), head_dim a multiple of 64, bf16 output, no
+ * activation; waits are bounded: a source that never reports leaves NaN in
+ * its slot and sets the device status.
+ */
+int tm_scaled_mm_i8_ulysses_exchange(const int8_t* a, const int8_t* b, const float* scale_a,
+                                     int64_t scale_a_numel, const float* scale_b,
+                                     int64_t scale_b_numel, const void* bias, int64_t m,
+                                     int64_t n, int64_t k, int64_t lda, int64_t ldb,
+                                     int num_heads, int head_dim, void* const* peer_recv,
+                                     void* const* peer_flags, int world, int rank,
+                                     uint32_t epoch, void* stream);
+
+/*
  * The row-parallel LoRA linears with their reduction fused into the kernel
  * (the reference's fused-row-reduce LoRA forward,
  * src/taomate_hd/inference/lora_checkpoint.py:127-143: each rank adds its

@@ -70,6 +70,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         c_int, [c_void_p, c_void_p, c_void_p, c_i64, c_void_p, c_i64, c_void_p,
                 c_void_p, c_i64, c_void_p, c_i64, c_int, c_i64, c_i64, c_i64, c_i64, c_i64,
                 c_void_p, c_void_p, c_void_p, c_int, c_int, c_u32, c_void_p]),
+    "tm_scaled_mm_i8_ulysses_exchange": (
+        c_int, [c_void_p, c_void_p, c_void_p, c_i64, c_void_p, c_i64, c_void_p, c_i64, c_i64,
+                c_i64, c_i64, c_i64, c_int, c_int, c_void_p, c_void_p, c_int, c_int, c_u32,
+                c_void_p]),
     "tm_lora_down_proj": (
         c_int, [c_void_p, c_i64, c_void_p, c_i64, c_void_p, c_i64, c_int, c_i64, c_i64, c_void_p]),
     "tm_scaled_mm_i8_lora": (

@@ -71,6 +71,13 @@ struct GemmArgs {
   // (the reference's _merged_qkv_send_layout, distributed/ulysses.py:153-193,
   // with its zero-padded head shards) instead of [M][N]; see ulysses_coords.
   int ul_world, ul_heads, ul_head_dim, ul_local;
+  // Ulysses exchange over NVLink (ul_peer != 0): instead of a local send
+  // buffer, each 64-column pass goes straight into destination rank w's
+  // receive buffer peer_part[w] ([ul_world][3][M][ul_local x head_dim], this
+  // rank's slot ul_rank); element counts per destination are added to
+  // peer_count[w][ul_rank], and the launch ends once this rank's counters
+  // show every source's rows (ul_uses x the source's element count).
+  int ul_peer, ul_rank, ul_uses;
   // Split-K (one-CTA kernel): each tile's K range is cut into `splits`
   // slices of kb_per_split k-blocks; every (tile, slice) unit stores its exact
   // int32 partial in ws[slice][M][N] and bumps tile_counters[tile]; the unit
@@ -283,6 +290,46 @@ __device__ __forceinline__ OutT* out_row_ptr(const GemmArgs& g, int64_t row) {
   return static_cast<OutT*>(g.out) + row * g.ldo;
 }
 
+// Ulysses send layout: output column `col` (a multiple of 32, never crossing
+// a head) of row `row` goes to the send buffer viewed as
+// [ul_world * 3 * M rows][ul_local * head_dim columns]: row
+// (w * 3 + qkv) * M + row, column (head % ul_local) * head_dim + d, with
+// qkv = col / (heads * head_dim), head = that part / head_dim and
+// w = head / ul_local.  Padded head slots (w * ul_local + h >= heads) are
+// never written here; the host zeroes them before the launch.
+__device__ __forceinline__ void ulysses_coords(const GemmArgs& g, int col, int64_t row, int& x,
+                                               int64_t& y) {
+  const int width = g.ul_heads * g.ul_head_dim;
+  const int qkv = col / width;
+  const int within = col - qkv * width;
+  const int head = within / g.ul_head_dim;
+  const int w = head / g.ul_local;
+  x = within - w * g.ul_local * g.ul_head_dim;
+  y = static_cast<int64_t>(w * 3 + qkv) * g.M + row;
+}
+
+// Ulysses exchange over NVLink: the destination rank of output column `col`
+// (a multiple of 64 inside one head) and the address of row 0 of that
+// column in the destination's receive buffer (row stride ul_local x
+// head_dim).
+__device__ __forceinline__ int ul_peer_dest(const GemmArgs& g, int col) {
+  const int width = g.ul_heads * g.ul_head_dim;
+  const int within = col - (col / width) * width;
+  return (within / g.ul_head_dim) / g.ul_local;
+}
+
+template <typename OutT>
+__device__ __forceinline__ OutT* ul_peer_base(const GemmArgs& g, int col) {
+  int x;
+  int64_t y;
+  ulysses_coords(g, col, 0, x, y);  // y = (w * 3 + qkv) * M for row 0
+  const int w = ul_peer_dest(g, col);
+  const int64_t qkv_rows = y - static_cast<int64_t>(w) * 3 * g.M;  // qkv * M
+  const int64_t ld = static_cast<int64_t>(g.ul_local) * g.ul_head_dim;
+  return reinterpret_cast<OutT*>(g.peer_part[w]) +
+         (static_cast<int64_t>(g.ul_rank) * 3 * g.M + qkv_rows) * ld + x;
+}
+
 // Per-warp staging tile: 32 rows x 128 bytes, 16-byte chunks XOR-swizzled by
 // row so that both the row-per-lane writes and the row-segment reads are
 // free of bank conflicts.
@@ -340,12 +387,18 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tmem_b
     const int chunks = pass_cols * static_cast<int>(sizeof(OutT)) / 16;  // 8 or 4 per row
     const int rows_per_store = 32 / chunks;
     const int chunk = lane % chunks;
+    // Ulysses exchange: the whole pass lies in one head of one destination
+    OutT* ul_base = (g.ul_peer && pass_col0 < g.N) ? ul_peer_base<OutT>(g, pass_col0) : nullptr;
+    const int64_t ul_ld = static_cast<int64_t>(g.ul_local) * g.ul_head_dim;
 #pragma unroll 1
     for (int rr = lane / chunks; rr < 32; rr += rows_per_store) {
       const int64_t out_r = row_base + rr;
       const int col = pass_col0 + chunk * (16 / static_cast<int>(sizeof(OutT)));
-      if (out_r < g.M && col < g.N)
-        *reinterpret_cast<uint4*>(out_row_ptr<OutT>(g, out_r) + col) = *stage_slot(stage, rr, chunk);
+      if (out_r < g.M && col < g.N) {
+        OutT* dst = ul_base != nullptr ? ul_base + out_r * ul_ld + (col - pass_col0)
+                                       : out_row_ptr<OutT>(g, out_r) + col;
+        *reinterpret_cast<uint4*>(dst) = *stage_slot(stage, rr, chunk);
+      }
     }
     __syncwarp();
   }
@@ -373,24 +426,6 @@ static_assert(kBiasCacheOffset + 256 <= kEpiStageBytes, "epilogue warp region");
 
 __device__ __forceinline__ uint4* stage64_slot(uint8_t* stage, int row, int chunk) {
   return reinterpret_cast<uint4*>(stage + row * 64 + ((chunk ^ ((row >> 1) & 3)) << 4));
-}
-
-// Ulysses send layout: output column `col` (a multiple of 32, never crossing
-// a head) of row `row` goes to the send buffer viewed as
-// [ul_world * 3 * M rows][ul_local * head_dim columns]: row
-// (w * 3 + qkv) * M + row, column (head % ul_local) * head_dim + d, with
-// qkv = col / (heads * head_dim), head = that part / head_dim and
-// w = head / ul_local.  Padded head slots (w * ul_local + h >= heads) are
-// never written here; the host zeroes them before the launch.
-__device__ __forceinline__ void ulysses_coords(const GemmArgs& g, int col, int64_t row, int& x,
-                                               int64_t& y) {
-  const int width = g.ul_heads * g.ul_head_dim;
-  const int qkv = col / width;
-  const int within = col - qkv * width;
-  const int head = within / g.ul_head_dim;
-  const int w = head / g.ul_local;
-  x = within - w * g.ul_local * g.ul_head_dim;
-  y = static_cast<int64_t>(w * 3 + qkv) * g.M + row;
 }
 
 // One lane's share of a tile's column constants: 4 scales, 4 bias values,
@@ -629,6 +664,21 @@ __device__ __forceinline__ void publish_counts(const GemmArgs& g, const long lon
   }
 }
 
+// Ulysses exchange: as publish_counts, to destination w's counter of this
+// source (peer_count[w][ul_rank]).
+__device__ __forceinline__ void publish_ul_counts(const GemmArgs& g, const long long* sent,
+                                                  int warp, int lane) {
+  asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
+  if (warp == 2 && lane == 0) {
+    __threadfence_system();
+    for (int w = 0; w < g.ul_world; ++w)
+      if (sent[w] > 0)
+        asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(g.peer_count[w] + g.ul_rank),
+                     "l"(static_cast<unsigned long long>(sent[w]))
+                     : "memory");
+  }
+}
+
 __device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
   unsigned long long v;
   asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
@@ -829,6 +879,47 @@ __device__ void reduce_phase(const GemmArgs& g, int bn, int cta, int ctas) {
       poison_owner_block(g, g.peer_out[g.rank] + static_cast<int64_t>(j) * g.rows_per_owner * g.N,
                          g.N, bn, cta, ctas);
   __syncthreads();
+}
+
+// Ulysses exchange, receiving side, run by one CTA after its tiles: wait
+// (bounded) until every source's counter shows its rows of the heads this
+// rank holds (3 x M x real heads x head_dim elements per call), so that the
+// launch ends with the receive buffer complete.  A source that never reports
+// leaves its slot overwritten with NaN and the device status set.
+__device__ void ulysses_wait_phase(const GemmArgs& g) {
+  const int real = max(0, min(g.ul_local, g.ul_heads - g.ul_rank * g.ul_local));
+  const unsigned long long target = static_cast<unsigned long long>(g.ul_uses) * 3ull *
+                                    static_cast<unsigned long long>(g.M) *
+                                    static_cast<unsigned long long>(real) *
+                                    static_cast<unsigned long long>(g.ul_head_dim);
+  __shared__ unsigned int ul_missing;
+  if (threadIdx.x == 0) ul_missing = 0u;
+  __syncthreads();
+  if (threadIdx.x < static_cast<unsigned>(g.ul_world)) {
+    const unsigned long long* c = g.peer_count[g.ul_rank] + threadIdx.x;
+    bool seen = ld_acquire_sys_u64(c) >= target;
+    if (!seen) {
+      const uint64_t t0 = globaltimer_ns();
+      while (!(seen = ld_acquire_sys_u64(c) >= target)) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+        __nanosleep(64);
+      }
+    }
+    if (!seen) {
+      if (g.status) atomicExch(g.status, kDevWaitTimeout);
+      atomicOr(&ul_missing, 1u << threadIdx.x);
+    }
+  }
+  __syncthreads();
+  const unsigned int lost = ul_missing;
+  if (lost == 0u) return;
+  const int64_t slot = 3ll * g.M * g.ul_local * g.ul_head_dim;  // elements per source slot
+  const uint4 nan8 = make_uint4(0x7fc07fc0u, 0x7fc07fc0u, 0x7fc07fc0u, 0x7fc07fc0u);
+  for (int s = 0; s < g.ul_world; ++s) {
+    if (!(lost & (1u << s))) continue;
+    uint4* dst = reinterpret_cast<uint4*>(g.peer_part[g.ul_rank] + s * slot);
+    for (int64_t v = threadIdx.x; v < slot / 8; v += blockDim.x) dst[v] = nan8;
+  }
 }
 
 // Write a staged 32-row x (chunks x 16 bytes) block back as row segments:
@@ -1439,6 +1530,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (g.world > 0 && row0 < g.M)
         sent[static_cast<int>(row0 / g.rows_per_owner)] += kBM * min(BN, g.N - nb * BN);
+      if (g.ul_peer && row0 < g.M) {  // elements this tile sent to each destination
+        const long long rows = min(static_cast<int64_t>(kBM), g.M - row0);
+        for (int c = nb * BN; c < min((nb + 1) * BN, g.N); c += 64) sent[ul_peer_dest(g, c)] += rows * 64;
+      }
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
@@ -1446,6 +1541,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (g.tma_store && lane == 0) bulk_wait_all();  // stores done before the CTA ends
     if (g.world > 0) publish_counts(g, sent, warp, lane);
+    if (g.ul_peer) publish_ul_counts(g, sent, warp, lane);
   }
 
   tc_fence_before();
@@ -1455,6 +1551,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_dealloc_pair(tmem_base, PairTmem<BN>::kCols);
   }
   if (g.world > 0) reduce_phase(g, BN, blockIdx.x, gridDim.x);
+  if (g.ul_peer && blockIdx.x == 0) ulysses_wait_phase(g);
 }
 
 // ====================================================================== CTA pair + LoRA
@@ -1917,7 +2014,7 @@ struct Operands {
 template <int BN, typename OutT>
 bool encode_out_map(CUtensorMap* map, GemmArgs& args) {
   memset(map, 0, sizeof(*map));
-  args.tma_store = args.world == 0 && args.splits == 1;
+  args.tma_store = args.world == 0 && args.splits == 1 && args.ul_peer == 0;
   if (!args.tma_store) return true;
   const CUtensorMapDataType dt = std::is_same<OutT, __nv_bfloat16>::value
                                      ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
@@ -2024,8 +2121,9 @@ int launch_pair(const Operands& op, GemmArgs args, int max_pairs, cudaStream_t s
   attr[1].id = cudaLaunchAttributeCooperative;
   attr[1].val.cooperative = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = args.world > 0 ? 2 : 1;
-  const cudaError_t err = args.world > 0 ? cudaLaunchKernelEx(&cfg, kernel, ta, tb, to, args)
+  const bool coop = args.world > 0 || args.ul_peer;
+  cfg.numAttrs = coop ? 2 : 1;
+  const cudaError_t err = coop ? cudaLaunchKernelEx(&cfg, kernel, ta, tb, to, args)
                                          : launch_with_pdl(cfg, attr, 1, kernel, ta, tb, to, args);
   if (err != cudaSuccess) return TM_ERR_CUDA;
   return check_launch();
@@ -2262,6 +2360,12 @@ struct ScatterSpec {
 // Ulysses send layout of a merged QKV projection.
 struct UlyssesSpec {
   int heads, head_dim, world;
+  // exchange over NVLink (peer_recv != nullptr): every rank's receive
+  // buffer and counters, this rank, and the call's use count
+  void* const* peer_recv = nullptr;
+  void* const* peer_flags = nullptr;
+  int rank = 0;
+  uint32_t epoch = 0;
 };
 
 // Optional split-K workspace (zeroed by the caller before its first use; the
@@ -2293,6 +2397,19 @@ int validate_scaled_mm(const void* out, int out_dtype, const int8_t* a, const in
     if (3LL * ul->world * m > 0x7fffffffLL) return TM_ERR_TOO_LARGE;
     if (swiglu || scatter != nullptr || lora != nullptr) return TM_ERR_UNSUPPORTED;
     ldo = n;  // the row-stride checks below see a [m, n] output; the layout is the send buffer
+    if (ul->peer_recv != nullptr) {  // exchange over NVLink
+      // a 64-column epilogue pass must stay inside one head (one destination)
+      if (ul->head_dim % 64 != 0) return TM_ERR_SHAPE;
+      if (ul->world > kMaxPeers) return TM_ERR_TOO_LARGE;
+      if (ul->rank < 0 || ul->rank >= ul->world) return TM_ERR_SHAPE;
+      if (out_dtype != TM_DTYPE_BF16 || epilogue != 0) return TM_ERR_UNSUPPORTED;
+      if (ul->peer_flags == nullptr) return TM_ERR_NULL_POINTER;
+      for (int j = 0; j < ul->world; ++j) {
+        if (!ul->peer_recv[j] || !ul->peer_flags[j]) return TM_ERR_NULL_POINTER;
+        if (!aligned16(ul->peer_recv[j]) || !aligned16(ul->peer_flags[j]))
+          return TM_ERR_ALIGNMENT;
+      }
+    }
   }
   // SwiGLU: n interleaved (gate, up) columns in, n / 2 columns out
   if (lda < k || ldb < k || ldo < (swiglu ? n / 2 : n)) return TM_ERR_SHAPE;
@@ -2363,6 +2480,15 @@ int scaled_mm_impl(void* out, int out_dtype, const int8_t* a, const int8_t* b, c
     args.ul_heads = ul->heads;
     args.ul_head_dim = ul->head_dim;
     args.ul_local = (ul->heads + ul->world - 1) / ul->world;
+    if (ul->peer_recv != nullptr) {
+      args.ul_peer = 1;
+      args.ul_rank = ul->rank;
+      args.ul_uses = static_cast<int>(ul->epoch);
+      for (int j = 0; j < ul->world; ++j) {
+        args.peer_part[j] = static_cast<__nv_bfloat16*>(ul->peer_recv[j]);
+        args.peer_count[j] = static_cast<unsigned long long*>(ul->peer_flags[j]);
+      }
+    }
   }
   if (scatter != nullptr) {
     args.world = scatter->world;
@@ -2384,6 +2510,9 @@ int scaled_mm_impl(void* out, int out_dtype, const int8_t* a, const int8_t* b, c
       ws != nullptr && ws->ptr != nullptr && scatter == nullptr && !swiglu && ul == nullptr;
   Choice choice = pick_choice(args.M, args.N, args.kblocks, sms, max_pairs, can_split);
   if (force_cfg) choice = Choice{force_cfg, 1};
+  // the exchange's generic-store epilogue and its counts run in the 256-wide
+  // pair kernel
+  if (args.ul_peer) choice = Choice{kPairFlag + 256, 1};
   if (can_split && ws->force_splits > 0) choice.splits = ws->force_splits;
   if (swiglu) {
     // the SwiGLU epilogue works in 64-column passes of each warp's half tile
@@ -2641,6 +2770,29 @@ int tm_scaled_mm_i8_ulysses_send(void* send, int out_dtype, const int8_t* a, con
     }
   }
   return TM_OK;
+}
+
+int tm_scaled_mm_i8_ulysses_exchange(const int8_t* a, const int8_t* b, const float* scale_a,
+                                     int64_t scale_a_numel, const float* scale_b,
+                                     int64_t scale_b_numel, const void* bias, int64_t m,
+                                     int64_t n, int64_t k, int64_t lda, int64_t ldb,
+                                     int num_heads, int head_dim, void* const* peer_recv,
+                                     void* const* peer_flags, int world, int rank,
+                                     uint32_t epoch, void* stream) {
+  if (peer_recv == nullptr || peer_flags == nullptr) return TM_ERR_NULL_POINTER;
+  if (world < 1 || world > tmw::kMaxPeers) return TM_ERR_TOO_LARGE;
+  if (rank < 0 || rank >= world) return TM_ERR_SHAPE;
+  if (peer_recv[rank] == nullptr) return TM_ERR_NULL_POINTER;
+  tmw::UlyssesSpec spec{num_heads, head_dim, world};
+  spec.peer_recv = peer_recv;
+  spec.peer_flags = peer_flags;
+  spec.rank = rank;
+  spec.epoch = epoch;
+  // `out` only has to pass the pointer checks: every store goes to a receive
+  // buffer through peer_recv
+  return tmw::scaled_mm_impl(peer_recv[rank], TM_DTYPE_BF16, a, b, scale_a, scale_a_numel,
+                             scale_b, scale_b_numel, bias, m, n, k, lda, ldb, n, 0u, nullptr, 0,
+                             tmw::as_stream(stream), nullptr, nullptr, nullptr, &spec);
 }
 
 int tm_scaled_mm_i8_workspace_size(int64_t m, int64_t n, int64_t k, uint64_t* bytes) {

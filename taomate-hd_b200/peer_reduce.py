@@ -71,10 +71,7 @@ class _PeerBuffers:
         self.check_every = check_every
         if world < 1 or world > 8:
             raise ValueError("the fused reduction supports 1..8 ranks")
-        if rows % (256 * world):
-            raise ValueError(f"rows ({rows}) must be a multiple of 256 * world ({256 * world})")
-        if cols % 16:
-            raise ValueError("cols must be a multiple of 16")
+        self._check_shape(rows, cols, world)
         self.ctx, self.rows, self.cols, self.device = ctx, rows, cols, device
         self.world, self.rank = world, rank
         self.rows_per_owner = rows // world
@@ -120,6 +117,13 @@ class _PeerBuffers:
                       for h in (0, 1)] if self._gather else None
         self.calls = 0
         self._uses = [0, 0]
+
+    @staticmethod
+    def _check_shape(rows: int, cols: int, world: int) -> None:
+        if rows % (256 * world):
+            raise ValueError(f"rows ({rows}) must be a multiple of 256 * world ({256 * world})")
+        if cols % 16:
+            raise ValueError("cols must be a multiple of 16")
 
     def _check(self, q: torch.Tensor, w_q: torch.Tensor) -> tuple[int, int]:
         m, k = q.shape

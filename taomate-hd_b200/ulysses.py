@@ -5,11 +5,16 @@ The reference's inference path (src/taomate_hd/distributed/ulysses.py:166-212,
 ``[tokens, 3 * heads * head_dim]`` output into the all-to-all send layout
 ``[world, 3, tokens, ceil(heads / world), head_dim]`` (zero heads pad the last
 shards when ``world`` does not divide ``heads``, ulysses.py:188-193) and
-exchanges it.  Here the
-scaled GEMM's epilogue writes the send layout directly
-(``torch.ops.taomate_w8a8.scaled_mm_i8_ulysses_send``), so the projection
-output is never materialised in token-major order; the exchange and the
-receive layout are the reference's.
+exchanges it.  Two forms here:
+
+* ``merged_qkv_sequence_to_heads_w8a8``: the scaled GEMM's epilogue writes
+  the send layout directly (``torch.ops.taomate_w8a8.scaled_mm_i8_ulysses_send``),
+  so the projection output is never materialised in token-major order; the
+  exchange is NCCL's all-to-all, and the receive layout the reference's.
+* ``PeerUlyssesExchange``: the epilogue stores each head block straight into
+  the receive buffer of the rank that holds the head, over NVLink
+  (``tm_scaled_mm_i8_ulysses_exchange``); the launch returns with every
+  rank's receive buffer complete, so there is no separate exchange.
 """
 from __future__ import annotations
 
@@ -73,3 +78,72 @@ def merged_qkv_sequence_to_heads_w8a8(q: torch.Tensor, q_scale: torch.Tensor, w_
     send = qkv_send_buffer(q, q_scale, w_q, w_scale, bias, num_heads=num_heads,
                            head_dim=head_dim, world=world)
     return exchange_qkv(send, group=group)
+
+
+class PeerUlyssesExchange:
+    """The merged QKV projection and its Ulysses all-to-all in one launch.
+
+    Per rank, two receive buffer sets ``[world, 3, tokens, local, head_dim]``
+    (``local = ceil(heads / world)``, zeroed once, so padded head slots stay
+    zero) and their counters, shared across ``group`` by CUDA IPC
+    (``peer_reduce``'s buffers).  Every rank calls with its own ``tokens``
+    rows, in the same order.  ``__call__`` returns the reference's
+    ``(q, k, v)``, each ``[tokens * world, local, head_dim]`` (copies; with
+    ``world == 1`` views valid until the second call after).  Waits inside
+    the kernel are bounded; :meth:`check` raises when one ran out.
+    """
+
+    def __init__(self, ctx, tokens: int, num_heads: int, head_dim: int,
+                 device: torch.device):
+        from .peer_reduce import _PeerBuffers
+
+        world = ctx.tp_world_size if ctx is not None else 1
+        self.world, self.tokens = world, tokens
+        self.num_heads, self.head_dim = num_heads, head_dim
+        self.local = -(-num_heads // world)
+
+        class _Buffers(_PeerBuffers):
+            @staticmethod
+            def _check_shape(rows: int, cols: int, world: int) -> None:
+                if tokens % 32:
+                    raise ValueError("tokens must be a multiple of 32")
+                if head_dim % 64:
+                    raise ValueError("head_dim must be a multiple of 64")
+
+        self._buf = _Buffers(ctx, world * 3 * tokens, self.local * head_dim, device)
+        self.rank = self._buf.rank
+        self.device = device
+
+    def __call__(self, q: torch.Tensor, q_scale: torch.Tensor, w_q: torch.Tensor,
+                 w_scale: torch.Tensor, bias: torch.Tensor | None) -> tuple[torch.Tensor, ...]:
+        """(q, k, v) of int8 ``q`` ([tokens, d], per-token scales) against int8
+        ``w_q`` ([3 * heads * head_dim, d], per-channel ``w_scale``)."""
+        if int(w_q.shape[0]) != 3 * self.num_heads * self.head_dim:
+            raise ValueError("merged QKV width differs from heads * head_dim")
+        if q.shape[0] != self.tokens or q.shape[1] != w_q.shape[1]:
+            raise ValueError("activation shape differs from the one the buffers were built for")
+        buf = self._buf
+        half, stream = buf._next_set()
+        m, k = q.shape
+        rc = buf._lib.tm_scaled_mm_i8_ulysses_exchange(
+            q.data_ptr(), w_q.data_ptr(), q_scale.data_ptr(), q_scale.numel(),
+            w_scale.data_ptr(), w_scale.numel(), None if bias is None else bias.data_ptr(),
+            m, w_q.shape[0], k, q.stride(0), w_q.stride(0), self.num_heads, self.head_dim,
+            buf._part[half], buf._counts[half], self.world, self.rank, buf._uses[half], stream)
+        if rc != 0:
+            buf._raise("tm_scaled_mm_i8_ulysses_exchange", rc)
+        buf._after_call()
+        from .peer_reduce import _wrap_bf16
+
+        flat = _wrap_bf16(buf._part[half][self.rank], self.world * 3 * self.tokens,
+                          self.local * self.head_dim, self.device)
+        received = flat.view(self.world, 3, self.tokens, self.local, self.head_dim)
+        if self.world == 1:
+            return tuple(received[0].unbind(0))
+        return receive_layout(received)
+
+    def check(self) -> None:
+        self._buf.check()
+
+    def close(self) -> None:
+        self._buf.close()

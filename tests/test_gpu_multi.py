@@ -219,6 +219,33 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
         ref = recv.movedim(0, 1).contiguous().view(3, tokens * world, heads // world, hd)
         torch.cuda.synchronize()
         ulysses_ok = all(torch.equal(a, b) for a, b in zip(got, ref.unbind(0)))
+        # the exchange done by the QKV epilogue over NVLink: the same (q, k, v)
+        # bit for bit as the NCCL path, over three calls, with 8 heads and with
+        # 9 (the last shard padded with a zero head)
+        from taomate_hd_b200.ulysses import PeerUlyssesExchange
+
+        for heads_x in (8, 9):
+            ex = PeerUlyssesExchange(ctx, tokens, heads_x, hd, device)
+            for call in range(3):
+                gx = torch.Generator(device=device).manual_seed(80 + 10 * call + rank)
+                qx2 = torch.randint(-127, 128, (tokens, d), generator=gx, device=device,
+                                    dtype=torch.int8)
+                gw2 = torch.Generator(device=device).manual_seed(90 + call)
+                wx2 = torch.randint(-127, 128, (3 * heads_x * hd, d), generator=gw2,
+                                    device=device, dtype=torch.int8)
+                sx2 = torch.rand(tokens, 1, generator=gx, device=device) * 1e-2
+                swx2 = torch.rand(3 * heads_x * hd, generator=gw2, device=device) * 1e-3
+                want = merged_qkv_sequence_to_heads_w8a8(qx2, sx2, wx2, swx2, None,
+                                                         num_heads=heads_x, head_dim=hd,
+                                                         group=group, world=world)
+                got2 = ex(qx2, sx2, wx2, swx2, None)
+                torch.cuda.synchronize()
+                ulysses_ok = ulysses_ok and all(
+                    torch.equal(a.view(torch.int16), b.view(torch.int16))
+                    for a, b in zip(got2, want))
+            ex.check()
+            torch.distributed.barrier()
+            ex.close()
         code = ctypes.c_int(-1)
         _native.capi().tm_device_status(rank, ctypes.byref(code), 1)
         result.update(ok=True, checks=checks, device_status=code.value, ulysses_ok=ulysses_ok)

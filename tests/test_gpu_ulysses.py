@@ -75,3 +75,48 @@ def test_send_layout_argument_errors(tm_ops, cuda):
     from taomate_hd_b200.ulysses import merged_qkv_sequence_to_heads_w8a8
     with pytest.raises(ValueError):  # the reference's width check
         merged_qkv_sequence_to_heads_w8a8(q2, sq2, w2, sw2, None, num_heads=4, head_dim=64)
+
+
+@pytest.mark.parametrize("tokens,d,heads", [(256, 512, 8), (320, 1024, 24), (2560, 3072, 24)])
+def test_nvlink_exchange_on_one_rank_matches_send_layout(tm_ops, cuda, tokens, d, heads):
+    """The exchange form (tm_scaled_mm_i8_ulysses_exchange) at one rank: the
+    kernel stores into its own receive buffer, counts its stores and waits
+    for them, so its (q, k, v) equal the send-layout path's bit for bit, over
+    three calls (both buffer sets, a second use of one)."""
+    from taomate_hd_b200.parallel import ParallelContext
+    from taomate_hd_b200.ulysses import PeerUlyssesExchange, merged_qkv_sequence_to_heads_w8a8
+
+    head_dim = 128
+    ex = PeerUlyssesExchange(ParallelContext(tp_world_size=1, tp_rank=0, tp_group=None), tokens,
+                             heads, head_dim, cuda)
+    try:
+        for call in range(3):
+            q, w, sq, sw, bias = _operands(tokens, d, 3 * heads * head_dim, seed=call + tokens,
+                                           cuda=cuda)
+            want = merged_qkv_sequence_to_heads_w8a8(q, sq, w, sw, bias, num_heads=heads,
+                                                     head_dim=head_dim)
+            got = ex(q, sq, w, sw, bias)
+            torch.cuda.synchronize()
+            for a, b in zip(got, want):
+                assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+        ex.check()
+    finally:
+        ex.close()
+
+
+def test_nvlink_exchange_argument_errors(capi, cuda):
+    """Host checks of the exchange entry point, before any launch."""
+    import ctypes
+
+    p = ctypes.c_void_p(1 << 20)
+    arr = (ctypes.c_void_p * 2)(p, p)
+    call = capi.tm_scaled_mm_i8_ulysses_exchange
+    #     a  b  sa  n   sb  n     bias  m    n     k    lda  ldb  heads hd   recv flags world rank ep st
+    assert call(p, p, p, 256, p, 3072, None, 256, 3072, 512, 512, 512, 8, 128, None, arr, 2, 0, 1,
+                None) == 1  # no receive buffers
+    assert call(p, p, p, 256, p, 3072, None, 256, 3072, 512, 512, 512, 8, 128, arr, arr, 9, 0, 1,
+                None) == 8  # more than 8 ranks
+    assert call(p, p, p, 256, p, 3072, None, 256, 3072, 512, 512, 512, 8, 128, arr, arr, 2, 2, 1,
+                None) == 2  # rank outside the group
+    assert call(p, p, p, 256, p, 1536, None, 256, 1536, 512, 512, 512, 16, 32, arr, arr, 2, 0, 1,
+                None) == 2  # head_dim not a multiple of 64
