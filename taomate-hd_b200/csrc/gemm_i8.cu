@@ -685,14 +685,19 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned 
   return v;
 }
 
-// Sum one block's partials from `world` (<= W) source slots, V vectors of 8
+// The owner-side reduction works in strips of kRedRows rows x one column
+// tile: at TP = 8 an owner's 1024 x 3072 block is then 384 work items for
+// the 148 CTAs instead of 96 128-row blocks of 512 KiB each.
+constexpr int kRedRows = 32;
+
+// Sum one strip's partials from `world` (<= W) source slots, V vectors of 8
 // columns per thread per round: all V x world 16-byte loads of a round are
 // issued before any is consumed, keeping ~32 registers of NVLink loads in
 // flight per thread (3-5 MB across the GPU, enough to keep NVLink busy).
 template <int V, int W>
 __device__ __forceinline__ void reduce_block(const GemmArgs& g, int lrb, int col0,
                                              int vec_per_row) {
-  const int total = kBM * vec_per_row;
+  const int total = kRedRows * vec_per_row;
   for (int v0 = threadIdx.x; v0 < total; v0 += V * blockDim.x) {
     uint4 raw[V][W];
     int64_t off[V];
@@ -701,7 +706,7 @@ __device__ __forceinline__ void reduce_block(const GemmArgs& g, int lrb, int col
       const int v = v0 + u * static_cast<int>(blockDim.x);
       const int vv = v < total ? v : v0;
       const int r = vv / vec_per_row;
-      off[u] = (static_cast<int64_t>(lrb) * kBM + r) * g.N + col0 + (vv - r * vec_per_row) * 8;
+      off[u] = (static_cast<int64_t>(lrb) * kRedRows + r) * g.N + col0 + (vv - r * vec_per_row) * 8;
     }
     const __nv_bfloat16* slots = g.peer_part[g.rank];
     const int64_t slot_elems = static_cast<int64_t>(g.rows_per_owner) * g.N;
@@ -746,14 +751,14 @@ __device__ __forceinline__ void reduce_block(const GemmArgs& g, int lrb, int col
 #pragma unroll
       for (int j = 0; j < 4; ++j) op[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
       if (g.peer_out[0] == nullptr) {
-        *reinterpret_cast<uint4*>(g.red_out + (static_cast<int64_t>(lrb) * kBM + r) * g.red_ldo +
+        *reinterpret_cast<uint4*>(g.red_out + (static_cast<int64_t>(lrb) * kRedRows + r) * g.red_ldo +
                                   c) = o;
       } else {
         // all-gather by push: this owner's rows into every rank's output,
         // starting with the next rank so that the ranks' stores spread
         // over the destinations
         const int64_t go = (static_cast<int64_t>(g.rank) * g.rows_per_owner +
-                            static_cast<int64_t>(lrb) * kBM + r) * g.N + c;
+                            static_cast<int64_t>(lrb) * kRedRows + r) * g.N + c;
 #pragma unroll
         for (int d = 1; d <= W; ++d)
           if (d <= g.world) {
@@ -773,16 +778,16 @@ __device__ __forceinline__ void reduce_block(const GemmArgs& g, int lrb, int col
 // nothing is written to a peer that may be gone.
 __device__ void poison_owner_block(const GemmArgs& g, __nv_bfloat16* block, int64_t ld, int bn,
                                    int cta, int ctas) {
-  const int tiles = (g.rows_per_owner / kBM) * g.num_n;
+  const int tiles = (g.rows_per_owner / kRedRows) * g.num_n;
   const uint4 nan8 = make_uint4(0x7fc07fc0u, 0x7fc07fc0u, 0x7fc07fc0u, 0x7fc07fc0u);
   for (int t = cta; t < tiles; t += ctas) {
     const int lrb = t / g.num_n;
     const int col0 = (t - lrb * g.num_n) * bn;
     const int vec_per_row = min(bn, g.N - col0) / 8;
-    for (int v = threadIdx.x; v < kBM * vec_per_row; v += blockDim.x) {
+    for (int v = threadIdx.x; v < kRedRows * vec_per_row; v += blockDim.x) {
       const int r = v / vec_per_row;
       const int c = col0 + (v - r * vec_per_row) * 8;
-      *reinterpret_cast<uint4*>(block + (static_cast<int64_t>(lrb) * kBM + r) * ld + c) = nan8;
+      *reinterpret_cast<uint4*>(block + (static_cast<int64_t>(lrb) * kRedRows + r) * ld + c) = nan8;
     }
   }
 }
@@ -796,7 +801,7 @@ __device__ void poison_owner_block(const GemmArgs& g, __nv_bfloat16* block, int6
 // HBM), sum in rank order in fp32, add the bias, store.  The wait is
 // bounded; a timeout records the device status and skips the reduction.
 __device__ void reduce_phase(const GemmArgs& g, int bn, int cta, int ctas) {
-  const int rbpo = g.rows_per_owner / kBM;
+  const int rbpo = g.rows_per_owner / kRedRows;
   const int tiles = rbpo * g.num_n;
   if (cta >= tiles) return;
   // Every source sends each element of this rank's rows_per_owner x N block
@@ -834,7 +839,7 @@ __device__ void reduce_phase(const GemmArgs& g, int bn, int cta, int ctas) {
     const int nb = t - lrb * g.num_n;
     const int col0 = nb * bn;
     const int vec_per_row = min(bn, g.N - col0) / 8;
-    reduced += static_cast<unsigned long long>(kBM) * vec_per_row * 8;
+    reduced += static_cast<unsigned long long>(kRedRows) * vec_per_row * 8;
     if (g.world <= 2)
       reduce_block<4, 2>(g, lrb, col0, vec_per_row);
     else if (g.world <= 4)
