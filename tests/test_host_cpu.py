@@ -189,6 +189,32 @@ def test_c_abi_host_argument_checks():
     assert args  # sizes used above
     tile = lib.tm_scaled_mm_i8_tile
     assert tile(p, 0, p, p, p, 128, p, 256, None, 128, 256, 512, 512, 512, 256, 0, None, 96, None) == capi_mod.TM_ERR_UNSUPPORTED
+    arr = (ctypes.c_void_p * 2)(p, p)
+    # fused row-parallel LoRA: LoRA operand checks, then the scatter checks
+    lrs = lib.tm_scaled_mm_i8_lora_reduce_scatter
+    lar = lib.tm_scaled_mm_i8_lora_all_reduce
+    #         out a  b  sa  n    sb  n    bias t  ldt lb ldlb r   m    n    k    lda  ldb  ldo  part flags w  rank ep st
+    assert lrs(p, p, p, p, 512, p, 768, None, p, 64, p, 64, 12, 512, 768, 256, 256, 256, 768, arr, arr,
+               2, 0, 1, None) == capi_mod.TM_ERR_UNSUPPORTED  # rank not a multiple of 8
+    assert lrs(p, p, p, p, 500, p, 768, None, p, 64, p, 64, 64, 500, 768, 256, 256, 256, 768, arr, arr,
+               2, 0, 1, None) == capi_mod.TM_ERR_SHAPE  # rows not a multiple of 256 x world
+    assert lrs(p, p, p, p, 512, p, 768, None, p, 64, p, 64, 64, 512, 768, 256, 256, 256, 768, arr, arr,
+               9, 0, 1, None) == capi_mod.TM_ERR_TOO_LARGE
+    assert lar(p, p, p, 512, p, 768, None, p, 64, p, 64, 64, 512, 768, 256, 256, 256, arr, arr, None,
+               2, 0, 1, None) == capi_mod.TM_ERR_NULL_POINTER  # no output buffers
+    assert lar(p, p, p, 512, p, 768, None, p, 60, p, 64, 64, 512, 768, 256, 256, 256, arr, arr, arr,
+               2, 0, 1, None) == capi_mod.TM_ERR_SHAPE  # ldt below the rank
+    # Ulysses exchange over NVLink
+    ux = lib.tm_scaled_mm_i8_ulysses_exchange
+    #        a  b  sa  n    sb  n     bias  m    n     k    lda  ldb  heads hd  recv flags w  rank ep st
+    assert ux(p, p, p, 256, p, 3072, None, 256, 3072, 512, 512, 512, 8, 128, None, arr, 2, 0, 1,
+              None) == capi_mod.TM_ERR_NULL_POINTER
+    assert ux(p, p, p, 256, p, 3072, None, 256, 3072, 512, 512, 512, 8, 128, arr, arr, 2, 2, 1,
+              None) == capi_mod.TM_ERR_SHAPE  # rank outside the group
+    assert ux(p, p, p, 256, p, 1536, None, 256, 1536, 512, 512, 512, 16, 32, arr, arr, 2, 0, 1,
+              None) == capi_mod.TM_ERR_SHAPE  # head_dim not a multiple of 64
+    assert ux(p, p, p, 250, p, 3072, None, 250, 3072, 512, 512, 512, 8, 128, arr, arr, 2, 0, 1,
+              None) == capi_mod.TM_ERR_SHAPE  # tokens not a multiple of 32
     down = lib.tm_lora_down_proj  # (t, ldt, x, ldx, a, lda, rank, m, k, stream)
     assert down(p, 64, p, 512, p, 512, 64, 0, 512, None) == capi_mod.TM_OK            # no rows
     assert down(p, 72, p, 512, p, 512, 72, 128, 512, None) == capi_mod.TM_ERR_UNSUPPORTED
