@@ -374,3 +374,58 @@ def test_long_k_raster_is_a_permutation(m, n, k, rows_per_mb, bn, world):
         # a wave of 74 pair tiles touches few A panels and stays in one N-group
         wave = tiles[:74]
         assert len({mb for mb, _ in wave}) <= -(-74 // min(group_n, num_n)) + 1
+
+
+def _ul_peer_address(col: int, row: int, src: int, m: int, heads: int, head_dim: int,
+                     world: int) -> tuple[int, int]:
+    """Restatement of the exchange epilogue's store address (ul_peer_dest,
+    ul_peer_base and the row offset in gemm_i8.cu): output column `col` of
+    token `row` on source rank `src` lands in destination `w`'s receive buffer
+    [world, 3, m, local x head_dim] at flat element `offset`."""
+    local = -(-heads // world)
+    width = heads * head_dim
+    qkv, within = divmod(col, width)
+    head = within // head_dim
+    w = head // local
+    x = within - w * local * head_dim
+    ld = local * head_dim
+    return w, ((src * 3 + qkv) * m + row) * ld + x
+
+
+@pytest.mark.parametrize("heads,head_dim,world,m", [(8, 128, 2, 64), (9, 128, 2, 32),
+                                                     (24, 128, 8, 32), (6, 64, 4, 32),
+                                                     (2, 128, 4, 32)])
+def test_ulysses_exchange_addresses_equal_send_layout_then_all_to_all(heads, head_dim, world, m):
+    """Every source's outputs land exactly where the reference's send layout
+    followed by all_to_all_single puts them (rank w receives chunk w of every
+    source, in source order), each real position once, padded heads never."""
+    from oracle import w8a8_oracle as orc
+
+    n = 3 * heads * head_dim
+    local = -(-heads // world)
+    # value[src][row, col] = a unique tag per (src, row, col)
+    tags = [torch.arange(m * n, dtype=torch.float64).reshape(m, n) + src * m * n
+            for src in range(world)]
+    # reference: send layout per source, then all-to-all (chunk w of src -> rank w, slot src)
+    sends = [orc.merged_qkv_send_layout(t, heads, head_dim, world) for t in tags]
+    want = [torch.stack([sends[src][w] for src in range(world)]) for w in range(world)]
+    got = [torch.full((world, 3, m, local, head_dim), -1.0, dtype=torch.float64)
+           for _ in range(world)]
+    flat = [g.view(-1) for g in got]
+    written = [torch.zeros(g.numel(), dtype=torch.int64) for g in got]
+    cols = torch.arange(n)
+    for src in range(world):
+        for row in range(m):
+            for c0 in range(0, n, 64):  # one address computation per 64-column pass
+                w, off = _ul_peer_address(c0, row, src, m, heads, head_dim, world)
+                flat[w][off:off + 64] = tags[src][row, c0:c0 + 64]
+                written[w][off:off + 64] += 1
+    assert cols.numel() == n
+    for w in range(world):
+        real = max(0, min(local, heads - w * local))
+        mask = torch.zeros(world, 3, m, local, head_dim, dtype=torch.bool)
+        mask[:, :, :, :real, :] = True
+        assert bool((written[w].view_as(mask)[mask] == 1).all())   # each real position once
+        assert bool((written[w].view_as(mask)[~mask] == 0).all())  # padded heads untouched
+        assert torch.equal(got[w][mask], want[w][mask])
+        assert bool((want[w][~mask] == 0).all())  # the reference pads with zero heads
