@@ -31,8 +31,14 @@ enum QuantMode : int {
   kWeight = 2,     // per-row amax/127 clamped at 1e-12, q = clamp(x / s, +-127)
   kModulate = 3,   // adaLN modulate, then dynamic
   kRmsModulate = 4,  // RMSNorm, adaLN modulate, then dynamic
-  kResGateRmsModulate = 5  // gated residual add, then as kRmsModulate
+  kResGateRmsModulate = 5,  // gated residual add, then as kRmsModulate
+  kModulateRows = 6  // kModulate with one table row per row (no index): tables loaded with x
 };
+
+// adaLN modulate without RMSNorm (indexed or per-row tables)
+__host__ __device__ constexpr bool modulate_only(int mode) {
+  return mode == kModulate || mode == kModulateRows;
+}
 
 struct QuantParams {
   const void* x;
@@ -309,7 +315,9 @@ __device__ __forceinline__ float rsqrt_two_step_rn(float v) {
 // caller quantises it as a plain bf16 row.  Table loads are plain read-only
 // loads the compiler can issue ahead of the stores.
 template <int VPT, int MODE>
-__device__ __forceinline__ void adaln_rows(const QuantParams& p, uint4 (&raw)[VPT], int64_t row,
+__device__ __forceinline__ void adaln_rows(const QuantParams& p, uint4 (&raw)[VPT],
+                                           const uint4 (&pre_sc)[VPT],
+                                           const uint4 (&pre_sh)[VPT], int64_t row,
                                            int t, int tpr, int64_t nvec, bool active,
                                            double* red) {
   constexpr int E = 8;
@@ -386,9 +394,10 @@ __device__ __forceinline__ void adaln_rows(const QuantParams& p, uint4 (&raw)[VP
     const int64_t vi = t + static_cast<int64_t>(i) * tpr;
     if (active && vi < nvec) {
       uint4 wr = make_uint4(0u, 0u, 0u, 0u);
-      if constexpr (MODE != kModulate) wr = ld_cached16(p.norm_w + vi * E);
-      const uint4 scr = ld_cached16(sc_row + vi * E);
-      const uint4 shr = ld_cached16(sh_row + vi * E);
+      if constexpr (!modulate_only(MODE)) wr = ld_cached16(p.norm_w + vi * E);
+      // per-row tables were loaded together with x
+      const uint4 scr = MODE == kModulateRows ? pre_sc[i] : ld_cached16(sc_row + vi * E);
+      const uint4 shr = MODE == kModulateRows ? pre_sh[i] : ld_cached16(sh_row + vi * E);
       uint32_t* xw = reinterpret_cast<uint32_t*>(&raw[i]);
       const uint32_t* ww = reinterpret_cast<const uint32_t*>(&wr);
       const uint32_t* cw = reinterpret_cast<const uint32_t*>(&scr);
@@ -396,7 +405,7 @@ __device__ __forceinline__ void adaln_rows(const QuantParams& p, uint4 (&raw)[VP
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         float2 x = unpack_bf16x2(xw[j]);
-        if constexpr (MODE != kModulate) {
+        if constexpr (!modulate_only(MODE)) {
           const float2 w = unpack_bf16x2(ww[j]);
           x.x = round_bf16(__fmul_rn(__fmul_rn(x.x, rinv), w.x));
           x.y = round_bf16(__fmul_rn(__fmul_rn(x.y, rinv), w.y));
@@ -435,8 +444,8 @@ __global__ void __launch_bounds__(256, (quant_min_blocks<MODE, VPT>())) quant_ro
   const int64_t nvec = p.cols / E;
   const T* xr = reinterpret_cast<const T*>(p.x) + (active ? row : 0) * p.ldx;
 
-  constexpr bool kAdaLN =
-      MODE == kModulate || MODE == kRmsModulate || MODE == kResGateRmsModulate;
+  constexpr bool kAdaLN = modulate_only(MODE) || MODE == kRmsModulate ||
+                          MODE == kResGateRmsModulate;
   static_assert(!kAdaLN || std::is_same<T, __nv_bfloat16>::value, "adaLN modes are bf16");
   if constexpr ((MODE == kDynamic || kAdaLN) && std::is_same<T, __nv_bfloat16>::value) {
     // Plain dynamic quant of bf16: the row maximum from packed bf16 pairs
@@ -452,7 +461,28 @@ __global__ void __launch_bounds__(256, (quant_min_blocks<MODE, VPT>())) quant_ro
       const int64_t vi = t + static_cast<int64_t>(i) * tpr;
       raw[i] = (active && vi < nvec) ? ld_stream16(xr + vi * E) : make_uint4(0u, 0u, 0u, 0u);
     }
-    if constexpr (kAdaLN) adaln_rows<VPT, MODE>(p, raw, row, t, tpr, nvec, active, red_f64);
+    // Modulate with per-row tables (the per-token adaLN of the BASELINE
+    // configuration): the row's shift / scale rows come from HBM like x, so
+    // they are loaded in the same burst and a row costs one memory round
+    // trip instead of two (768p, 20480 x 3072: 121 -> 107 us).  Indexed
+    // tables stay cache-resident and keep the lighter register set (loading
+    // them early measured 74 -> 86 us); the RMSNorm modes need the row's
+    // reduction first.
+    uint4 pre_sc[VPT], pre_sh[VPT];
+    if constexpr (MODE == kModulateRows) {
+      const int64_t trow = active ? row : 0;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int64_t vi = t + static_cast<int64_t>(i) * tpr;
+        const bool in = active && vi < nvec;
+        pre_sc[i] = in ? ld_cached16(p.mod_scale + trow * p.table_stride + vi * E)
+                       : make_uint4(0u, 0u, 0u, 0u);
+        pre_sh[i] = in ? ld_cached16(p.shift + trow * p.table_stride + vi * E)
+                       : make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+    if constexpr (kAdaLN)
+      adaln_rows<VPT, MODE>(p, raw, pre_sc, pre_sh, row, t, tpr, nvec, active, red_f64);
     __nv_bfloat162 m2 = __float2bfloat162_rn(0.0f), n2 = m2;
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
@@ -688,7 +718,7 @@ int launch_modulate(QuantParams p, cudaStream_t stream) {
   if (p.cols % 8 != 0 || p.table_stride % 8 != 0 || !aligned16(p.x) || !aligned16(p.q) ||
       !aligned16(p.shift) || !aligned16(p.mod_scale) ||
       (p.hidden_out != nullptr && !aligned16(p.hidden_out)) ||
-      (MODE != kModulate && !aligned16(p.norm_w)) ||
+      (!modulate_only(MODE) && !aligned16(p.norm_w)) ||
       (MODE == kResGateRmsModulate &&
        (!aligned16(p.branch) || !aligned16(p.gate) || !aligned16(p.residual_out))))
     return TM_ERR_ALIGNMENT;
@@ -701,7 +731,7 @@ int launch_modulate(QuantParams p, cudaStream_t stream) {
   // layout (59 against 65 us).
   int tpr_log2 = 0, vpt = 0;
   const int64_t nvec = p.cols / 8;
-  if (MODE != kModulate && nvec <= 32 * 12) {
+  if (!modulate_only(MODE) && nvec <= 32 * 12) {
     tpr_log2 = 5;
     vpt = static_cast<int>((nvec + 31) / 32);
   } else if (!pick_layout(nvec, &tpr_log2, &vpt)) {
@@ -783,7 +813,8 @@ int tm_modulate_int8_quant(int8_t* out, float* scales, void* hidden_out, const v
   p.table_stride = table_stride;
   p.rows = rows;
   p.cols = cols;
-  return tmw::launch_modulate<tmw::kModulate>(p, tmw::as_stream(stream));
+  return index == nullptr ? tmw::launch_modulate<tmw::kModulateRows>(p, tmw::as_stream(stream))
+                          : tmw::launch_modulate<tmw::kModulate>(p, tmw::as_stream(stream));
 }
 
 int tm_rms_norm_modulate_int8_quant(int8_t* out, float* scales, void* hidden_out,
