@@ -486,8 +486,9 @@ def ulysses_exchange(ctx, world: int, device: torch.device, flush: torch.Tensor)
     bias = (torch.randn(n, generator=g, device=device) * 0.01).to(torch.bfloat16)
     a = torch.randint(-127, 128, (m, D), generator=g, device=device, dtype=torch.int8)
     sa = torch.rand(m, 1, generator=g, device=device) * 1e-2 + 1e-4
-    ex = PeerUlyssesExchange(ctx, m, HEADS, HEAD_DIM, device)
-    group = ctx.tp_group
+    group = ctx.tp_group  # the bench's Ulysses degree is its GPU count
+    ex = PeerUlyssesExchange(m, HEADS, HEAD_DIM, device, group=group, world=world,
+                             rank=ctx.tp_rank)
     fused = _timed(lambda: ex(a, sa, w, sw, bias), 10, flush, world, device)
     nccl = _timed(lambda: merged_qkv_sequence_to_heads_w8a8(
         a, sa, w, sw, bias, num_heads=HEADS, head_dim=HEAD_DIM, group=group, world=world),

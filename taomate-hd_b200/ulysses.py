@@ -83,21 +83,24 @@ def merged_qkv_sequence_to_heads_w8a8(q: torch.Tensor, q_scale: torch.Tensor, w_
 class PeerUlyssesExchange:
     """The merged QKV projection and its Ulysses all-to-all in one launch.
 
-    Per rank, two receive buffer sets ``[world, 3, tokens, local, head_dim]``
+    Per rank of the Ulysses ``group`` (``world`` ranks, this one ``rank``;
+    the reference passes the group to ``merged_qkv_sequence_to_heads``),
+    two receive buffer sets ``[world, 3, tokens, local, head_dim]``
     (``local = ceil(heads / world)``, zeroed once, so padded head slots stay
-    zero) and their counters, shared across ``group`` by CUDA IPC
+    zero) and their counters, shared across the group by CUDA IPC
     (``peer_reduce``'s buffers).  Every rank calls with its own ``tokens``
     rows, in the same order.  ``__call__`` returns the reference's
     ``(q, k, v)``, each ``[tokens * world, local, head_dim]`` (copies; with
     ``world == 1`` views valid until the second call after).  Waits inside
     the kernel are bounded; :meth:`check` raises when one ran out.
+    :meth:`from_context` takes the Ulysses axis of a ``ParallelContext``.
     """
 
-    def __init__(self, ctx, tokens: int, num_heads: int, head_dim: int,
-                 device: torch.device):
+    def __init__(self, tokens: int, num_heads: int, head_dim: int, device: torch.device, *,
+                 group=None, world: int = 1, rank: int = 0):
+        from .parallel import ParallelContext
         from .peer_reduce import _PeerBuffers
 
-        world = ctx.tp_world_size if ctx is not None else 1
         self.world, self.tokens = world, tokens
         self.num_heads, self.head_dim = num_heads, head_dim
         self.local = -(-num_heads // world)
@@ -110,9 +113,20 @@ class PeerUlyssesExchange:
                 if head_dim % 64:
                     raise ValueError("head_dim must be a multiple of 64")
 
-        self._buf = _Buffers(ctx, world * 3 * tokens, self.local * head_dim, device)
-        self.rank = self._buf.rank
+        # the buffer machinery is written over a TP-style context: here the
+        # Ulysses group plays that role
+        axis = ParallelContext(tp_world_size=world, tp_rank=rank, tp_group=group)
+        self._buf = _Buffers(axis, world * 3 * tokens, self.local * head_dim, device)
+        self.rank = rank
         self.device = device
+
+    @classmethod
+    def from_context(cls, ctx, tokens: int, num_heads: int, head_dim: int,
+                     device: torch.device) -> "PeerUlyssesExchange":
+        """Over the Ulysses axis of ``ctx`` (``ulysses_group``,
+        ``ulysses_world_size``, ``ulysses_rank``)."""
+        return cls(tokens, num_heads, head_dim, device, group=ctx.ulysses_group,
+                   world=ctx.ulysses_world_size, rank=ctx.ulysses_rank)
 
     def __call__(self, q: torch.Tensor, q_scale: torch.Tensor, w_q: torch.Tensor,
                  w_scale: torch.Tensor, bias: torch.Tensor | None) -> tuple[torch.Tensor, ...]:

@@ -225,7 +225,8 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
         from taomate_hd_b200.ulysses import PeerUlyssesExchange
 
         for heads_x in (8, 9):
-            ex = PeerUlyssesExchange(ctx, tokens, heads_x, hd, device)
+            ex = PeerUlyssesExchange(tokens, heads_x, hd, device, group=group, world=world,
+                                     rank=rank)
             for call in range(3):
                 gx = torch.Generator(device=device).manual_seed(80 + 10 * call + rank)
                 qx2 = torch.randint(-127, 128, (tokens, d), generator=gx, device=device,

@@ -87,8 +87,7 @@ def test_nvlink_exchange_on_one_rank_matches_send_layout(tm_ops, cuda, tokens, d
     from taomate_hd_b200.ulysses import PeerUlyssesExchange, merged_qkv_sequence_to_heads_w8a8
 
     head_dim = 128
-    ex = PeerUlyssesExchange(ParallelContext(tp_world_size=1, tp_rank=0, tp_group=None), tokens,
-                             heads, head_dim, cuda)
+    ex = PeerUlyssesExchange.from_context(ParallelContext(), tokens, heads, head_dim, cuda)
     try:
         for call in range(3):
             q, w, sq, sw, bias = _operands(tokens, d, 3 * heads * head_dim, seed=call + tokens,

@@ -429,3 +429,20 @@ def test_ulysses_exchange_addresses_equal_send_layout_then_all_to_all(heads, hea
         assert bool((written[w].view_as(mask)[~mask] == 0).all())  # padded heads untouched
         assert torch.equal(got[w][mask], want[w][mask])
         assert bool((want[w][~mask] == 0).all())  # the reference pads with zero heads
+
+
+@pytest.mark.parametrize("tokens,head_dim,match", [(250, 128, "multiple of 32"),
+                                                   (256, 96, "multiple of 64")])
+def test_ulysses_exchange_rejects_unsupported_shapes_before_allocating(tokens, head_dim, match):
+    """The NVLink exchange's shape rules raise before any buffer is allocated,
+    through the explicit-group constructor and through a ParallelContext's
+    Ulysses axis."""
+    from taomate_hd_b200.parallel import ParallelContext
+    from taomate_hd_b200.ulysses import PeerUlyssesExchange
+
+    with pytest.raises(ValueError, match=match):
+        PeerUlyssesExchange(tokens, 8, head_dim, torch.device("cpu"), group=object(), world=2,
+                            rank=1)
+    ctx = ParallelContext(ulysses_world_size=2, ulysses_rank=0, ulysses_group=object())
+    with pytest.raises(ValueError, match=match):
+        PeerUlyssesExchange.from_context(ctx, tokens, 8, head_dim, torch.device("cpu"))
