@@ -5,7 +5,7 @@
 // Replaces vLLM's cutlass_scaled_mm as called by the reference
 // (src/taomate_hd/inference/w8a8.py:72 and :142-144).
 //
-// Two persistent, warp-specialised kernels share one epilogue:
+// Three persistent, warp-specialised kernels share one epilogue:
 //
 //   gemm_i8_pair_kernel  CTA pairs (clusters of 2).  A pair owns a 256 x BN
 //     output tile: each CTA fetches its 128 rows of A and BN/2 rows of B into
@@ -15,6 +15,8 @@
 //     2/3 of the operand bytes of a 128 x 256 one-CTA tile for the same MMA
 //     work, which is what lets the tensor pipe run near its rate from L2.
 //   gemm_i8_kernel       one CTA per tile of 128 x BN (small or ragged shapes).
+//   gemm_i8_pair_lora_kernel  the 256 x 256 pair tile with the bf16 LoRA delta
+//     added on the tensor cores between two epilogue passes.
 //
 // Warp roles (320 threads per CTA):
 //   warp 0      TMA producer: a STAGES-deep ring of (A, B) k-blocks of 128
@@ -25,8 +27,13 @@
 //               32*(w%4)..+31) and column half (w-2)/4; fp32 dequant
 //               sa * (sb * acc) (+ bias) (+ GELU-tanh) -> bf16/fp16 stores.
 // With two accumulators the epilogue of one tile overlaps the main loop of
-// the next.  Tiles are visited in groups of 16 M-blocks for L2 reuse; tails
-// use TMA zero fill and predicated stores.  Every wait is bounded (ptx.cuh).
+// the next.  Tiles are visited in groups of 16 M-blocks for L2 reuse (or in
+// N-fastest groups when K is long); tails use TMA zero fill and predicated
+// stores.  Outputs go to local memory by TMA stores, or, as 128-byte row
+// segments over NVLink, to the rows' owners (the fused reduce-scatter /
+// all-reduce, followed by the owner-side reduction in the same launch) or to
+// the heads' ranks (the Ulysses exchange).  Non-cooperative launches use
+// programmatic dependent launch.  Every wait is bounded (ptx.cuh).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
