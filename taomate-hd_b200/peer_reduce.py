@@ -58,6 +58,26 @@ def _wrap_bf16(ptr: int, rows: int, cols: int, device: torch.device) -> torch.Te
     return t.view(torch.bfloat16)
 
 
+def _check_lora(lora_t: torch.Tensor, lora_b: torch.Tensor, rows: int, cols: int) -> int:
+    """The LoRA operands of the fused row-parallel linears: ``lora_t`` bf16
+    ``[rows, r]`` and ``lora_b`` bf16 ``[cols, r]`` on CUDA, rows contiguous,
+    r in {8, 16, ..., 64}.  The kernel's tensor maps assume these extents,
+    so they are checked here before any launch.  Returns r."""
+    for name, t in (("lora_t", lora_t), ("lora_b", lora_b)):
+        if getattr(t, "dtype", None) != torch.bfloat16 or t.dim() != 2:
+            raise ValueError(f"{name} must be a 2-D bfloat16 tensor")
+        if t.device.type != "cuda":
+            raise RuntimeError(f"{name} must be a CUDA tensor")
+        if t.stride(1) != 1:
+            raise ValueError(f"{name} rows must be contiguous")
+    r = lora_t.shape[1]
+    if lora_t.shape[0] != rows or tuple(lora_b.shape) != (cols, r):
+        raise ValueError(f"lora_t must be [{rows}, r] and lora_b [{cols}, r]")
+    if r < 8 or r > 64 or r % 8:
+        raise ValueError("the LoRA rank must be a multiple of 8 up to 64")
+    return r
+
+
 class _PeerBuffers:
     """Two buffer sets per rank, shared across the TP group by CUDA IPC."""
 
@@ -216,7 +236,7 @@ class PeerReduceScatter(_PeerBuffers):
         m, k = self._check(q, w_q)
         if out.shape != (self.rows_per_owner, self.cols) or out.dtype != torch.bfloat16:
             raise ValueError(f"out must be bf16 [{self.rows_per_owner}, {self.cols}]")
-        r = lora_t.shape[1]
+        r = _check_lora(lora_t, lora_b, m, self.cols)
         half, stream = self._next_set()
         rc = self._lib.tm_scaled_mm_i8_lora_reduce_scatter(
             out.data_ptr(), q.data_ptr(), w_q.data_ptr(), q_scale.data_ptr(), q_scale.numel(),
@@ -271,7 +291,7 @@ class PeerAllReduce(_PeerBuffers):
         every rank; returns ``[rows, cols]`` (valid until the second call
         after this one)."""
         m, k = self._check(q, w_q)
-        r = lora_t.shape[1]
+        r = _check_lora(lora_t, lora_b, m, self.cols)
         half, stream = self._next_set()
         rc = self._lib.tm_scaled_mm_i8_lora_all_reduce(
             q.data_ptr(), w_q.data_ptr(), q_scale.data_ptr(), q_scale.numel(),

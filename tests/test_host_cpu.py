@@ -446,3 +446,38 @@ def test_ulysses_exchange_rejects_unsupported_shapes_before_allocating(tokens, h
     ctx = ParallelContext(ulysses_world_size=2, ulysses_rank=0, ulysses_group=object())
     with pytest.raises(ValueError, match=match):
         PeerUlyssesExchange.from_context(ctx, tokens, 8, head_dim, torch.device("cpu"))
+
+
+def test_peer_lora_operands_are_checked_before_any_launch():
+    """The fused row-parallel LoRA calls refuse LoRA operands whose extents
+    differ from the ones the kernel's tensor maps assume (a shorter lora_t
+    would be read past its end), before anything reaches the device."""
+    from taomate_hd_b200.peer_reduce import _check_lora
+
+    with pytest.raises(RuntimeError, match="CUDA"):  # host tensors
+        _check_lora(torch.empty(512, 64, dtype=torch.bfloat16),
+                    torch.empty(768, 64, dtype=torch.bfloat16), 512, 768)
+
+    class _Cuda:  # tensor metadata of a CUDA tensor; never dereferenced
+        def __init__(self, shape, dtype=torch.bfloat16, stride1=1):
+            self.shape, self.dtype = torch.Size(shape), dtype
+            self.device = torch.device("cuda", 0)
+            self._stride1 = stride1
+
+        def dim(self):
+            return len(self.shape)
+
+        def stride(self, i):
+            return self._stride1
+
+    assert _check_lora(_Cuda((512, 64)), _Cuda((768, 64)), 512, 768) == 64
+    with pytest.raises(ValueError, match=r"lora_t must be \[512, r\]"):
+        _check_lora(_Cuda((256, 64)), _Cuda((768, 64)), 512, 768)
+    with pytest.raises(ValueError, match="lora_t must be"):
+        _check_lora(_Cuda((512, 64)), _Cuda((768, 32)), 512, 768)
+    with pytest.raises(ValueError, match="multiple of 8"):
+        _check_lora(_Cuda((512, 12)), _Cuda((768, 12)), 512, 768)
+    with pytest.raises(ValueError, match="bfloat16"):
+        _check_lora(_Cuda((512, 64), torch.float16), _Cuda((768, 64)), 512, 768)
+    with pytest.raises(ValueError, match="contiguous"):
+        _check_lora(_Cuda((512, 64), stride1=2), _Cuda((768, 64)), 512, 768)
