@@ -58,6 +58,41 @@ def _wrap_bf16(ptr: int, rows: int, cols: int, device: torch.device) -> torch.Te
     return t.view(torch.bfloat16)
 
 
+def _require_cuda(t, name: str) -> None:
+    if getattr(t, "device", None) is None or t.device.type != "cuda":
+        raise RuntimeError(f"{name} must be a CUDA tensor")
+
+
+def _check_operands(q: torch.Tensor, q_scale: torch.Tensor, w_q: torch.Tensor,
+                    w_scale: torch.Tensor, bias: torch.Tensor | None, rows: int,
+                    cols: int) -> tuple[int, int]:
+    """The GEMM operands of the fused calls, checked before anything reaches
+    the device (the kernels read ``rows`` token scales or one, ``cols``
+    channel scales or one, and ``cols`` bias values): ``q`` int8
+    ``[rows, k]`` and ``w_q`` int8 ``[cols, k]`` with contiguous rows, fp32
+    contiguous scales, bf16 contiguous bias, all on CUDA.  Returns (rows, k)."""
+    for t, name in ((q, "q"), (w_q, "w_q")):
+        if getattr(t, "dtype", None) != torch.int8 or t.dim() != 2:
+            raise ValueError(f"{name} must be a 2-D int8 tensor")
+        _require_cuda(t, name)
+        if t.stride(1) != 1:
+            raise ValueError(f"{name} rows must be contiguous")
+    m, k = q.shape
+    if m != rows or w_q.shape[0] != cols or w_q.shape[1] != k:
+        raise ValueError("shape differs from the one the buffers were built for")
+    for t, name, n in ((q_scale, "q_scale", rows), (w_scale, "w_scale", cols)):
+        if (getattr(t, "dtype", None) != torch.float32 or not t.is_contiguous()
+                or t.numel() not in (1, n)):
+            raise ValueError(f"{name} must be contiguous float32 with 1 or {n} values")
+        _require_cuda(t, name)
+    if bias is not None:
+        if (getattr(bias, "dtype", None) != torch.bfloat16 or not bias.is_contiguous()
+                or bias.numel() != cols):
+            raise ValueError(f"bias must be contiguous bfloat16 with {cols} values")
+        _require_cuda(bias, "bias")
+    return m, k
+
+
 def _check_lora(lora_t: torch.Tensor, lora_b: torch.Tensor, rows: int, cols: int) -> int:
     """The LoRA operands of the fused row-parallel linears: ``lora_t`` bf16
     ``[rows, r]`` and ``lora_b`` bf16 ``[cols, r]`` on CUDA, rows contiguous,
@@ -66,8 +101,7 @@ def _check_lora(lora_t: torch.Tensor, lora_b: torch.Tensor, rows: int, cols: int
     for name, t in (("lora_t", lora_t), ("lora_b", lora_b)):
         if getattr(t, "dtype", None) != torch.bfloat16 or t.dim() != 2:
             raise ValueError(f"{name} must be a 2-D bfloat16 tensor")
-        if t.device.type != "cuda":
-            raise RuntimeError(f"{name} must be a CUDA tensor")
+        _require_cuda(t, name)
         if t.stride(1) != 1:
             raise ValueError(f"{name} rows must be contiguous")
     r = lora_t.shape[1]
@@ -145,11 +179,9 @@ class _PeerBuffers:
         if cols % 16:
             raise ValueError("cols must be a multiple of 16")
 
-    def _check(self, q: torch.Tensor, w_q: torch.Tensor) -> tuple[int, int]:
-        m, k = q.shape
-        if m != self.rows or w_q.shape[0] != self.cols or w_q.shape[1] != k:
-            raise ValueError("shape differs from the one the buffers were built for")
-        return m, k
+    def _check(self, q: torch.Tensor, q_scale: torch.Tensor, w_q: torch.Tensor,
+               w_scale: torch.Tensor, bias: torch.Tensor | None) -> tuple[int, int]:
+        return _check_operands(q, q_scale, w_q, w_scale, bias, self.rows, self.cols)
 
     def _next_set(self) -> tuple[int, ctypes.c_void_p]:
         self.calls += 1
@@ -209,7 +241,7 @@ class PeerReduceScatter(_PeerBuffers):
         (or one) scales; ``w_q``: int8 ``[cols, k]`` local weight shard;
         ``w_scale``: fp32 ``[cols]``; ``bias``: bf16 ``[cols]`` or None.
         """
-        m, k = self._check(q, w_q)
+        m, k = self._check(q, q_scale, w_q, w_scale, bias)
         if out.shape != (self.rows_per_owner, self.cols) or out.dtype != torch.bfloat16:
             raise ValueError(f"out must be bf16 [{self.rows_per_owner}, {self.cols}]")
         half, stream = self._next_set()
@@ -233,7 +265,7 @@ class PeerReduceScatter(_PeerBuffers):
         owners, which sum in rank order and add ``bias`` once.  ``lora_t`` bf16
         ``[rows, r]`` (this rank's ``x_local A_local^T``), ``lora_b`` bf16
         ``[cols, r]`` carrying the adapter scale."""
-        m, k = self._check(q, w_q)
+        m, k = self._check(q, q_scale, w_q, w_scale, bias)
         if out.shape != (self.rows_per_owner, self.cols) or out.dtype != torch.bfloat16:
             raise ValueError(f"out must be bf16 [{self.rows_per_owner}, {self.cols}]")
         r = _check_lora(lora_t, lora_b, m, self.cols)
@@ -271,7 +303,7 @@ class PeerAllReduce(_PeerBuffers):
                  w_scale: torch.Tensor, bias: torch.Tensor | None,
                  tile_n: int = 0) -> torch.Tensor:
         """``[rows, cols] = (sum over ranks of q @ w_q^T) + bias`` on every rank."""
-        m, k = self._check(q, w_q)
+        m, k = self._check(q, q_scale, w_q, w_scale, bias)
         half, stream = self._next_set()
         rc = self._lib.tm_scaled_mm_i8_all_reduce(
             q.data_ptr(), w_q.data_ptr(), q_scale.data_ptr(), q_scale.numel(),
@@ -290,7 +322,7 @@ class PeerAllReduce(_PeerBuffers):
         :meth:`PeerReduceScatter.lora`, then every owner's reduced rows reach
         every rank; returns ``[rows, cols]`` (valid until the second call
         after this one)."""
-        m, k = self._check(q, w_q)
+        m, k = self._check(q, q_scale, w_q, w_scale, bias)
         r = _check_lora(lora_t, lora_b, m, self.cols)
         half, stream = self._next_set()
         rc = self._lib.tm_scaled_mm_i8_lora_all_reduce(

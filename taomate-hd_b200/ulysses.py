@@ -132,10 +132,12 @@ class PeerUlyssesExchange:
                  w_scale: torch.Tensor, bias: torch.Tensor | None) -> tuple[torch.Tensor, ...]:
         """(q, k, v) of int8 ``q`` ([tokens, d], per-token scales) against int8
         ``w_q`` ([3 * heads * head_dim, d], per-channel ``w_scale``)."""
+        from .peer_reduce import _check_operands
+
         if int(w_q.shape[0]) != 3 * self.num_heads * self.head_dim:
             raise ValueError("merged QKV width differs from heads * head_dim")
-        if q.shape[0] != self.tokens or q.shape[1] != w_q.shape[1]:
-            raise ValueError("activation shape differs from the one the buffers were built for")
+        _check_operands(q, q_scale, w_q, w_scale, bias, self.tokens,
+                        3 * self.num_heads * self.head_dim)
         buf = self._buf
         half, stream = buf._next_set()
         m, k = q.shape

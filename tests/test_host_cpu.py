@@ -481,3 +481,52 @@ def test_peer_lora_operands_are_checked_before_any_launch():
         _check_lora(_Cuda((512, 64), torch.float16), _Cuda((768, 64)), 512, 768)
     with pytest.raises(ValueError, match="contiguous"):
         _check_lora(_Cuda((512, 64), stride1=2), _Cuda((768, 64)), 512, 768)
+
+
+def test_peer_gemm_operands_are_checked_before_any_launch():
+    """The fused calls (reduce-scatter, all-reduce, their LoRA forms, the
+    Ulysses exchange) refuse operands whose dtype, layout or length differ
+    from what the kernels read, before anything reaches the device."""
+    from taomate_hd_b200.peer_reduce import _check_operands
+
+    class _T:  # tensor metadata of a CUDA tensor; never dereferenced
+        def __init__(self, shape, dtype, contiguous=True, stride1=1, device="cuda"):
+            self.shape, self.dtype = torch.Size(shape), dtype
+            self.device = torch.device(device, 0) if device == "cuda" else torch.device(device)
+            self._c, self._s1 = contiguous, stride1
+
+        def dim(self):
+            return len(self.shape)
+
+        def stride(self, i):
+            return self._s1
+
+        def is_contiguous(self):
+            return self._c
+
+        def numel(self):
+            n = 1
+            for d in self.shape:
+                n *= d
+            return n
+
+    i8, f32, bf = torch.int8, torch.float32, torch.bfloat16
+    ok = dict(q=_T((512, 256), i8), q_scale=_T((512, 1), f32), w_q=_T((768, 256), i8),
+              w_scale=_T((768,), f32), bias=_T((768,), bf))
+    assert _check_operands(**ok, rows=512, cols=768) == (512, 256)
+    assert _check_operands(**{**ok, "bias": None, "q_scale": _T((1,), f32)},
+                           rows=512, cols=768) == (512, 256)
+    bad = [({"q": _T((512, 256), bf)}, ValueError, "int8"),
+           ({"q": _T((512, 256), i8, device="cpu")}, RuntimeError, "CUDA"),
+           ({"w_q": _T((768, 256), i8, stride1=2)}, ValueError, "contiguous"),
+           ({"w_q": _T((768, 128), i8)}, ValueError, "shape differs"),
+           ({"q": _T((256, 256), i8)}, ValueError, "shape differs"),
+           ({"q_scale": _T((256, 1), f32)}, ValueError, "q_scale"),
+           ({"w_scale": _T((768,), bf)}, ValueError, "w_scale"),
+           ({"w_scale": _T((768,), f32, contiguous=False)}, ValueError, "w_scale"),
+           ({"bias": _T((512,), bf)}, ValueError, "bias"),
+           ({"bias": _T((768,), torch.float16)}, ValueError, "bias"),
+           ({"bias": _T((768,), bf, device="cpu")}, RuntimeError, "CUDA")]
+    for change, exc, match in bad:
+        with pytest.raises(exc, match=match):
+            _check_operands(**{**ok, **change}, rows=512, cols=768)
