@@ -171,6 +171,7 @@ class _PeerBuffers:
                       for h in (0, 1)] if self._gather else None
         self.calls = 0
         self._uses = [0, 0]
+        self._failed = False
 
     @staticmethod
     def _check_shape(rows: int, cols: int, world: int) -> None:
@@ -184,12 +185,16 @@ class _PeerBuffers:
         return _check_operands(q, q_scale, w_q, w_scale, bias, self.rows, self.cols)
 
     def _next_set(self) -> tuple[int, ctypes.c_void_p]:
+        if self._failed:
+            raise RuntimeError("an earlier call on these buffers failed on this rank, so its "
+                               "call count no longer matches the other ranks'; build new buffers")
         self.calls += 1
         half = self.calls & 1
         self._uses[half] += 1
         return half, ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
 
     def _raise(self, name: str, rc: int) -> None:
+        self._failed = True
         raise RuntimeError(f"{name} failed: {self._lib.tm_status_string(rc).decode()}")
 
     def _after_call(self) -> None:
@@ -201,6 +206,9 @@ class _PeerBuffers:
         inside one of this library's kernels ran out since the status word was
         last cleared (a peer that never contributed: the rows it should have
         produced hold NaN).  The word is left as it is."""
+        # the status word is read by a blocking copy on the legacy stream, which
+        # does not wait for work on non-blocking streams: synchronise first
+        torch.cuda.synchronize(self.device)
         code = ctypes.c_int(0)
         index = self.device.index if self.device.index is not None else torch.cuda.current_device()
         rc = self._lib.tm_device_status(index, ctypes.byref(code), 0)
@@ -232,6 +240,13 @@ class _PeerBuffers:
 class PeerReduceScatter(_PeerBuffers):
     """Symmetric receive buffers + the fused GEMM/reduce-scatter for one shape."""
 
+    def _check_out(self, out: torch.Tensor) -> None:
+        if (tuple(out.shape) != (self.rows_per_owner, self.cols)
+                or getattr(out, "dtype", None) != torch.bfloat16 or out.stride(1) != 1):
+            raise ValueError(f"out must be bf16 [{self.rows_per_owner}, {self.cols}] "
+                             "with contiguous rows")
+        _require_cuda(out, "out")
+
     def __call__(self, q: torch.Tensor, q_scale: torch.Tensor, w_q: torch.Tensor,
                  w_scale: torch.Tensor, bias: torch.Tensor | None, out: torch.Tensor,
                  tile_n: int = 0) -> torch.Tensor:
@@ -242,8 +257,7 @@ class PeerReduceScatter(_PeerBuffers):
         ``w_scale``: fp32 ``[cols]``; ``bias``: bf16 ``[cols]`` or None.
         """
         m, k = self._check(q, q_scale, w_q, w_scale, bias)
-        if out.shape != (self.rows_per_owner, self.cols) or out.dtype != torch.bfloat16:
-            raise ValueError(f"out must be bf16 [{self.rows_per_owner}, {self.cols}]")
+        self._check_out(out)
         half, stream = self._next_set()
         rc = self._lib.tm_scaled_mm_i8_reduce_scatter(
             out.data_ptr(), q.data_ptr(), w_q.data_ptr(), q_scale.data_ptr(), q_scale.numel(),
@@ -266,8 +280,7 @@ class PeerReduceScatter(_PeerBuffers):
         ``[rows, r]`` (this rank's ``x_local A_local^T``), ``lora_b`` bf16
         ``[cols, r]`` carrying the adapter scale."""
         m, k = self._check(q, q_scale, w_q, w_scale, bias)
-        if out.shape != (self.rows_per_owner, self.cols) or out.dtype != torch.bfloat16:
-            raise ValueError(f"out must be bf16 [{self.rows_per_owner}, {self.cols}]")
+        self._check_out(out)
         r = _check_lora(lora_t, lora_b, m, self.cols)
         half, stream = self._next_set()
         rc = self._lib.tm_scaled_mm_i8_lora_reduce_scatter(

@@ -530,3 +530,39 @@ def test_peer_gemm_operands_are_checked_before_any_launch():
     for change, exc, match in bad:
         with pytest.raises(exc, match=match):
             _check_operands(**{**ok, **change}, rows=512, cols=768)
+
+
+def test_peer_reduce_scatter_output_and_failed_call_latch():
+    """The reduce-scatter output must be this rank's bf16 [rows/world, cols]
+    block with contiguous rows on CUDA; after a native call fails on one rank
+    its call count no longer matches the other ranks', so the buffers refuse
+    further calls instead of pairing this rank's next call with the wrong
+    call of its peers."""
+    from types import SimpleNamespace
+
+    from taomate_hd_b200.peer_reduce import PeerReduceScatter, _PeerBuffers
+
+    class _Out:  # tensor metadata; never dereferenced
+        def __init__(self, shape, dtype=torch.bfloat16, stride1=1, device="cuda"):
+            self.shape, self.dtype, self._s1 = torch.Size(shape), dtype, stride1
+            self.device = torch.device(device, 0) if device == "cuda" else torch.device(device)
+
+        def stride(self, i):
+            return self._s1
+
+    me = SimpleNamespace(rows_per_owner=256, cols=768)
+    PeerReduceScatter._check_out(me, _Out((256, 768)))
+    for out, exc in ((_Out((512, 768)), ValueError), (_Out((256, 768), torch.float16), ValueError),
+                     (_Out((256, 768), stride1=2), ValueError),
+                     (_Out((256, 768), device="cpu"), RuntimeError)):
+        with pytest.raises(exc):
+            PeerReduceScatter._check_out(me, out)
+
+    lib = SimpleNamespace(tm_status_string=lambda rc: b"CUDA error")
+    bufs = SimpleNamespace(_failed=False, calls=0, _uses=[0, 0], _lib=lib)
+    with pytest.raises(RuntimeError, match="CUDA error"):
+        _PeerBuffers._raise(bufs, "tm_scaled_mm_i8_reduce_scatter", 5)
+    assert bufs._failed and bufs.calls == 0
+    with pytest.raises(RuntimeError, match="earlier call"):
+        _PeerBuffers._next_set(bufs)
+    assert bufs.calls == 0 and bufs._uses == [0, 0]
