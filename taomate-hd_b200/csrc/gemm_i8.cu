@@ -2567,15 +2567,6 @@ int scaled_mm_impl(void* out, int out_dtype, const int8_t* a, const int8_t* b, c
 
 }  // namespace
 
-// ---------------------------------------------------------------------------
-// Allocation-free split-K (tm_scaled_mm_i8_splitk_noalloc).
-//
-// Scratch for callers that must not allocate device memory: a fixed array in
-// the library's own device image, present on every GPU that loads the
-// library until the process exits.  Host code may not use the array's name as
-// a pointer (on the host it is only a stand-in for the symbol); its device
-// address is looked up once per device with cudaGetSymbolAddress while that
-// device is current.
 // Host checks of the LoRA operands shared by the LoRA entry points.
 int check_lora(const void* lora_t, int64_t ldt, const void* lora_b, int64_t ldlb, int lora_rank,
                int64_t m) {
@@ -2587,6 +2578,15 @@ int check_lora(const void* lora_t, int64_t ldt, const void* lora_b, int64_t ldlb
   return TM_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free split-K (tm_scaled_mm_i8_splitk_noalloc).
+//
+// Scratch for callers that must not allocate device memory: a fixed array in
+// the library's own device image, present on every GPU that loads the
+// library until the process exits.  Host code may not use the array's name as
+// a pointer (on the host it is only a stand-in for the symbol); its device
+// address is looked up once per device with cudaGetSymbolAddress while that
+// device is current.
 constexpr uint64_t kNoAllocScratchBytes = TM_SPLITK_NOALLOC_MAX_BYTES;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
