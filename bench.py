@@ -10,8 +10,9 @@ group.  The TP degree equals the GPU count (strong scaling: the total work
 is fixed).  Metric: whole-job int8 TOPS = 2 * (2 M d ffn) / step time.
 
 Timing: W untimed warm-up steps; K timed steps, each bracketed by CUDA events
-on the launching stream, with a 256 MiB buffer written between steps to
-flush L2 (outside the events); barrier + synchronize around the timed region;
+on the launching stream, with L2 flushed between steps outside the events (a
+256 MiB buffer written, then another 256 MiB read, so that no dirty flush
+lines are written back inside the next step); barrier + synchronize around the timed region;
 the max over ranks is reported.  ``e2e`` repeats the step through the same
 public API with the input copied from pinned host memory and the output read
 back each step.
@@ -164,6 +165,27 @@ def barrier(world: int) -> None:
         torch.distributed.barrier()
 
 
+class L2Flush:
+    """Empties L2 (126 MB) of anything a timed launch could reuse: writes one
+    256 MiB buffer, then reads another.  The read matters: after the write
+    alone, L2 is full of the flush's dirty lines, and their write-back to HBM
+    would land inside the next timed region (about 126 MB, ~20 us of HBM
+    time that belongs to no kernel being measured).  ``write_only`` is the
+    write alone (the end-to-end loop, whose region holds the flush itself)."""
+
+    def __init__(self, device: torch.device):
+        self.dirty = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=device)
+        self.clean = torch.ones(FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+        self.sink = torch.empty((), dtype=torch.float32, device=device)
+
+    def __call__(self) -> None:
+        self.dirty.zero_()
+        torch.sum(self.clean, dim=0, out=self.sink)
+
+    def write_only(self) -> None:
+        self.dirty.zero_()
+
+
 # ----------------------------------------------------------------- CPU reference
 def cpu_reference_setup(rows: int, seed: int = 0):
     """Oracle operands for ``rows`` tokens of the workload at TP=1."""
@@ -291,7 +313,7 @@ STACK_BLOCKS = 40
 
 
 def lora_block_stack(ctx, device: torch.device, g: torch.Generator, world: int,
-                     flush: torch.Tensor) -> dict:
+                     flush: L2Flush) -> dict:
     """40 chained 768p blocks (QKV, out-proj, fc1, fc2) with
     the BF16 LoRA (rank 64, alpha 64) in the W8A8 epilogue and adaLN modulate
     fused into the activation quant; each block has its own weights, so every
@@ -313,7 +335,7 @@ def lora_block_stack(ctx, device: torch.device, g: torch.Generator, world: int,
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
               for _ in range(reps)]
         for e0, e1 in ev:
-            flush.zero_()
+            flush()
             e0.record()
             stack.forward(x)
             e1.record()
@@ -348,7 +370,7 @@ SWEEP_M = (64, 256, 1024, 4096, 16384, 32768)
 SWEEP_NK = ((3072, 3072), (12288, 3072))  # (N, K)
 
 
-def skinny_sweep(world: int, device: torch.device, flush: torch.Tensor) -> list[dict]:
+def skinny_sweep(world: int, device: torch.device, flush: L2Flush) -> list[dict]:
     """the scaled GEMM over M at two weight shapes.
 
     Each rank runs the column-parallel shard (N / TP) of its own weight; no
@@ -356,9 +378,9 @@ def skinny_sweep(world: int, device: torch.device, flush: torch.Tensor) -> list[
     measurements per shape:
 
     * ``us``: each launch timed alone with CUDA events (median of 10).
-      Before each, L2 is flushed by writing 256 MiB and then reading another
-      256 MiB, so the weights come from HBM and no dirty flush lines are left
-      for the timed kernel to write back (at small M that would dominate).
+      Before each, L2 is flushed (``L2Flush``), so the weights come from HBM
+      and no dirty flush lines are left for the timed kernel to write back
+      (at small M that would dominate).
     * ``stream_us``: 64 launches back to back on one stream, each on its own
       copy of the weight (the copies together exceed twice the L2), timed as
       one region and divided by the launch count: the per-layer time of a
@@ -370,8 +392,6 @@ def skinny_sweep(world: int, device: torch.device, flush: torch.Tensor) -> list[
     from taomate_hd_b200 import ops
 
     g = torch.Generator(device=device).manual_seed(77)
-    clean = torch.ones(FLUSH_BYTES // 4, dtype=torch.float32, device=device)
-    sink = torch.empty((), dtype=torch.float32, device=device)
     rows = []
     reps, chain = 10, 64
     for n_full, k in SWEEP_NK:
@@ -393,8 +413,7 @@ def skinny_sweep(world: int, device: torch.device, flush: torch.Tensor) -> list[
             ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                   for _ in range(reps)]
             for e0, e1 in ev:
-                flush.zero_()
-                torch.sum(clean, dim=0, out=sink)
+                flush()
                 e0.record()
                 ops.scaled_mm(a, ws[0].t(), sa, sb, torch.bfloat16, out=y)
                 e1.record()
@@ -402,8 +421,7 @@ def skinny_sweep(world: int, device: torch.device, flush: torch.Tensor) -> list[
             us = 1e3 * max_over_ranks(statistics.median(e0.elapsed_time(e1) for e0, e1 in ev),
                                       world, device)
             s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            flush.zero_()
-            torch.sum(clean, dim=0, out=sink)
+            flush()
             s0.record()
             for i in range(chain):
                 ops.scaled_mm(a, ws[i % copies].t(), sa, sb, torch.bfloat16, out=y)
@@ -420,7 +438,7 @@ def skinny_sweep(world: int, device: torch.device, flush: torch.Tensor) -> list[
     return rows
 
 
-def ulysses_send(device: torch.device, flush: torch.Tensor) -> list[dict]:
+def ulysses_send(device: torch.device, flush: L2Flush) -> list[dict]:
     """768p merged QKV projection per Ulysses rank (tokens / degree rows,
     all heads), written in the all-to-all send layout.
 
@@ -460,7 +478,7 @@ def ulysses_send(device: torch.device, flush: torch.Tensor) -> list[dict]:
             ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                   for _ in range(reps)]
             for e0, e1 in ev:
-                flush.zero_()
+                flush()
                 e0.record()
                 fn()
                 e1.record()
@@ -471,7 +489,7 @@ def ulysses_send(device: torch.device, flush: torch.Tensor) -> list[dict]:
     return rows
 
 
-def ulysses_exchange(ctx, world: int, device: torch.device, flush: torch.Tensor) -> dict:
+def ulysses_exchange(ctx, world: int, device: torch.device, flush: L2Flush) -> dict:
     """768p merged QKV projection and its Ulysses all-to-all at degree = N
     (tokens / N rows per rank, all heads): the exchange done by the GEMM's
     epilogue over NVLink (``PeerUlyssesExchange``) against the send-layout
@@ -506,7 +524,7 @@ def ulysses_exchange(ctx, world: int, device: torch.device, flush: torch.Tensor)
             "bit_identical": same}
 
 
-def _timed(fn, reps: int, flush: torch.Tensor, world: int, device) -> float:
+def _timed(fn, reps: int, flush: L2Flush, world: int, device) -> float:
     """Median device time (ms) of ``fn`` over ``reps`` calls, L2 flushed before
     each, barrier-separated, max over ranks."""
     for _ in range(2):
@@ -514,7 +532,7 @@ def _timed(fn, reps: int, flush: torch.Tensor, world: int, device) -> float:
     torch.cuda.synchronize()
     times = []
     for _ in range(reps):
-        flush.zero_()
+        flush()
         barrier(world)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
@@ -602,7 +620,7 @@ def multi_gpu_parity(mlp, world: int, rank: int, device, samples: int = 48) -> d
                          "NCCL bf16 ring: (world + 2) * 2^-8 * (sum |partial| + |bias| + |ref|)"}
 
 
-def reduce_vs_nccl(ctx, world: int, rank: int, device, flush: torch.Tensor) -> list[dict]:
+def reduce_vs_nccl(ctx, world: int, rank: int, device, flush: L2Flush) -> list[dict]:
     """The row-parallel GEMM with its reduction, fused over NVLink against the
     GEMM followed by NCCL, at this GPU count: 480p fc2 with a reduce-scatter
     (8192 x 3072 x 12288 / t) and the 768p out-projection with an all-reduce
@@ -668,7 +686,7 @@ def reduce_vs_nccl(ctx, world: int, rank: int, device, flush: torch.Tensor) -> l
     return out_rows
 
 
-def library_baselines(device, flush: torch.Tensor) -> dict:
+def library_baselines(device, flush: L2Flush) -> dict:
     """The library bars on this GPU, timed like our kernels: cuBLAS's int8 GEMM
     (``torch._int_mm``, int32 out) alone and followed by the same fp32
     dequant + bias (+ GELU) epilogue in torch, at the fc1 and fc2 shapes, next
@@ -755,11 +773,11 @@ def run_ours(args) -> int:
     outliers = torch.randperm(D, generator=g, device=device)[: max(1, D // 1000)]
     x[:, outliers] *= 20
     x = x.to(torch.bfloat16)
-    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=device)
+    flush = L2Flush(device)
 
     for _ in range(args.warmup):
         mlp.forward(x)
-        flush.zero_()
+        flush()
     torch.cuda.synchronize()
     barrier(world)
 
@@ -772,7 +790,7 @@ def run_ours(args) -> int:
         barrier(world)
         wall0 = time.perf_counter()
         for i in range(K):
-            flush.zero_()
+            flush()
             starts[i].record()
             mlp.forward(x, gemm_ev[i])
             ends[i].record()
@@ -820,7 +838,7 @@ def run_ours(args) -> int:
             up.wait_event(x_free[b])
             (x_part[b] if world > 1 else x_dev[b]).copy_(x_host, non_blocking=True)
             x_ready[b].record(up)
-        flush.zero_()
+        flush.write_only()
         main.wait_event(x_ready[b])
         if world > 1:
             torch.distributed.all_gather_into_tensor(x_dev[b], x_part[b])
@@ -914,7 +932,8 @@ def run_ours(args) -> int:
                        "reduce": ("none (TP=1)" if world == 1 else
                                   "fused into the fc2 GEMM epilogue (NVLink peer stores)"
                                   if args.reduce == "fused" else "nccl reduce_scatter_tensor"),
-                       "l2": "flushed between steps (256 MiB write outside the step events)"},
+                       "l2": "flushed between steps outside the step events (256 MiB written, "
+                             "then another 256 MiB read: no dirty flush lines left)"},
             "pct_int8_peak": 100.0 * value / (world * peak_int8),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_int8,
                          "unit": "TOPS", "frac": achieved / peak_int8, "traffic": traffic,
@@ -936,7 +955,8 @@ def run_ours(args) -> int:
                     "h2d_bytes_per_step": world * x_host.numel() * x_host.element_size(),
                     "d2h_bytes_per_step": world * y_host[0].numel() * y_host[0].element_size(),
                     "pipelining": "upload and read-back on their own streams, double-buffered; "
-                                  "L2 flushed inside the region before each step; N > 1: each "
+                                  "L2 flushed inside the region before each step (256 MiB "
+                                  "write); N > 1: each "
                                   "rank uploads its row slice, NCCL all-gather of the input"},
             "gpu_launches": K * launches,
             "wall_s_timed_region": wall,

@@ -6,6 +6,7 @@ import json
 import contextlib
 
 import pytest
+import torch
 
 import bench
 
@@ -106,3 +107,17 @@ def test_peaks_have_the_roofline_denominators():
     assert peaks["source"] in ("measured", "fallback")
     assert peaks["hbm_gbs"] > 1000 and peaks["bf16_tflops"] > 500
     assert peaks["bf16_tflops_sustained"] <= peaks["bf16_tflops"] * 1.05
+
+
+def test_l2_flush_writes_then_reads(monkeypatch):
+    monkeypatch.setattr(bench, "FLUSH_BYTES", 1 << 20)
+    flush = bench.L2Flush(torch.device("cpu"))
+    assert flush.dirty.numel() * flush.dirty.element_size() == 1 << 20
+    assert flush.clean.numel() * flush.clean.element_size() == 1 << 20
+    flush.dirty.fill_(7)
+    flush()
+    assert int(flush.dirty.max()) == 0 and float(flush.sink) == flush.clean.numel()
+    flush.dirty.fill_(7)
+    flush.sink.fill_(-1)
+    flush.write_only()
+    assert int(flush.dirty.max()) == 0 and float(flush.sink) == -1
