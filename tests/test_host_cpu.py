@@ -566,3 +566,29 @@ def test_peer_reduce_scatter_output_and_failed_call_latch():
     with pytest.raises(RuntimeError, match="earlier call"):
         _PeerBuffers._next_set(bufs)
     assert bufs.calls == 0 and bufs._uses == [0, 0]
+
+
+def test_documented_api_names_exist():
+    """Every operator, class, torch op and C entry point that INTEGRATION.md
+    and README.md tell a user to call exists under that name."""
+    import re
+    from pathlib import Path
+
+    import taomate_hd_b200.ops as ops_mod
+    import taomate_hd_b200.peer_reduce as peer_mod
+    import taomate_hd_b200.ulysses as ulysses_mod
+
+    root = Path(__file__).resolve().parents[1]
+    text = (root / "INTEGRATION.md").read_text() + (root / "README.md").read_text()
+    modules = {"ops": ops_mod, "ulysses": ulysses_mod, "peer_reduce": peer_mod}
+    missing = [f"{m}.{name}"
+               for m, name in re.findall(r"(?<![\w.])(ops|ulysses|peer_reduce)\.([A-Za-z_]\w*)", text)
+               if name != "py" and not hasattr(modules[m], name)]
+    for name in set(re.findall(r"torch\.ops\.taomate_w8a8\.(\w+)", text)):
+        try:
+            getattr(torch.ops.taomate_w8a8, name)
+        except (AttributeError, RuntimeError):
+            missing.append(f"torch.ops.taomate_w8a8.{name}")
+    header = (root / "include" / "taomate_w8a8.h").read_text()
+    missing += [name for name in set(re.findall(r"\btm_\w+", text)) if name not in header]
+    assert not missing, missing
