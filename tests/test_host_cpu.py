@@ -574,16 +574,22 @@ def test_documented_api_names_exist():
     import re
     from pathlib import Path
 
+    import taomate_hd_b200.dit as dit_mod
+    import taomate_hd_b200.fused_kernels as fused_mod
     import taomate_hd_b200.ops as ops_mod
     import taomate_hd_b200.peer_reduce as peer_mod
     import taomate_hd_b200.ulysses as ulysses_mod
 
     root = Path(__file__).resolve().parents[1]
     text = (root / "INTEGRATION.md").read_text() + (root / "README.md").read_text()
-    modules = {"ops": ops_mod, "ulysses": ulysses_mod, "peer_reduce": peer_mod}
-    missing = [f"{m}.{name}"
-               for m, name in re.findall(r"(?<![\w.])(ops|ulysses|peer_reduce)\.([A-Za-z_]\w*)", text)
+    modules = {"ops": ops_mod, "ulysses": ulysses_mod, "peer_reduce": peer_mod, "dit": dit_mod,
+               "fused_kernels": fused_mod}
+    pattern = r"(?<![\w.])(ops|ulysses|peer_reduce|dit|fused_kernels)\.([A-Za-z_]\w*)"
+    missing = [f"{m}.{name}" for m, name in re.findall(pattern, text)
                if name != "py" and not hasattr(modules[m], name)]
+    for name in ("TPW8A8AttnProj", "TPW8A8LoRABlockStack"):  # listed after dit.TPW8A8MLP
+        if name in text and not hasattr(dit_mod, name):
+            missing.append(f"dit.{name}")
     for name in set(re.findall(r"torch\.ops\.taomate_w8a8\.(\w+)", text)):
         try:
             getattr(torch.ops.taomate_w8a8, name)
