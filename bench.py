@@ -167,11 +167,11 @@ def barrier(world: int) -> None:
 
 class L2Flush:
     """Empties L2 (126 MB) of anything a timed launch could reuse: writes one
-    256 MiB buffer, then reads another.  The read matters: after the write
-    alone, L2 is full of the flush's dirty lines, and their write-back to HBM
-    would land inside the next timed region (about 126 MB, ~20 us of HBM
-    time that belongs to no kernel being measured).  ``write_only`` is the
-    write alone (the end-to-end loop, whose region holds the flush itself)."""
+    256 MiB buffer, then reads another.  After the write alone L2 may hold the
+    flush's dirty lines, whose write-back to HBM could land inside the next
+    timed launch; after the read it holds only clean lines of a buffer no
+    timed kernel touches.  ``write_only`` is the write alone (the end-to-end
+    loop, whose region holds the flush itself)."""
 
     def __init__(self, device: torch.device):
         self.dirty = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=device)
