@@ -109,3 +109,72 @@ def test_a_source_that_never_reports_makes_the_wait_run_out():
     for r in range(world):
         assert ranks[r].status == 1
         assert np.isnan(results[(r, 1)]).all()
+
+
+def test_all_reduce_output_stays_valid_until_the_second_call_after():
+    """The all-reduce adds a gather: each owner stores its reduced rows into
+    every rank's output of the call's set and bumps that rank's gather counter
+    (set, owner); a rank returns once every owner's rows are there.  The
+    output of call c must stay intact until this rank makes call c + 2 (the
+    host API's contract): another rank can only write this set again for call
+    c + 2, which needs this rank's own partials of call c + 2."""
+    world, calls, rows, cols = 4, 8, 2, 2
+    for seed in range(6):
+        outs = [np.zeros((2, world * rows, cols)) for _ in range(world)]
+        gather = [np.zeros((2, world), dtype=np.int64) for _ in range(world)]
+        slots = [np.zeros((2, world, rows, cols)) for _ in range(world)]
+        counts = [np.zeros((2, world), dtype=np.int64) for _ in range(world)]
+        locks = [threading.Lock() for _ in range(world)]
+        bad: list[str] = []
+
+        def wait(lock, arr, h, target):
+            t0 = time.monotonic()
+            while time.monotonic() - t0 < 5.0:
+                with lock:
+                    if bool((arr[h] >= target).all()):
+                        return True
+                time.sleep(1e-5)
+            return False
+
+        def worker(me: int):
+            rng = random.Random(seed * 31 + me)
+            uses = [0, 0]
+            kept: dict[int, np.ndarray] = {}
+            for call in range(1, calls + 1):
+                h = call & 1
+                if call - 2 in kept and not np.array_equal(outs[me][h], kept[call - 2]):
+                    bad.append(f"rank {me}: output of call {call - 2} changed before call {call}")
+                uses[h] += 1
+                for d in range(world):
+                    j = (me + 1 + d) % world
+                    time.sleep(rng.random() * 2e-4)
+                    slots[j][h, me] = _partial(call, me, j, rows, cols)
+                    with locks[j]:
+                        counts[j][h, me] += rows * cols
+                if not wait(locks[me], counts[me], h, uses[h] * rows * cols):
+                    bad.append(f"rank {me}: partial wait ran out")
+                    return
+                reduced = slots[me][h].sum(axis=0)
+                for d in range(world):
+                    j = (me + 1 + d) % world
+                    time.sleep(rng.random() * 2e-4)
+                    outs[j][h, me * rows:(me + 1) * rows] = reduced
+                    with locks[j]:
+                        gather[j][h, me] += rows * cols
+                if not wait(locks[me], gather[me], h, uses[h] * rows * cols):
+                    bad.append(f"rank {me}: gather wait ran out")
+                    return
+                want = np.concatenate([sum(_partial(call, s, o, rows, cols) for s in range(world))
+                                       for o in range(world)])
+                if not np.array_equal(outs[me][h], want):
+                    bad.append(f"rank {me}: call {call} output wrong")
+                kept[call] = outs[me][h].copy()
+                time.sleep(rng.random() * 4e-4)  # the caller still reads the output
+
+        threads = [threading.Thread(target=worker, args=(r,)) for r in range(world)]
+        for t in threads:
+            t.start()
+        for t in threads:
+            t.join(timeout=60)
+        assert not any(t.is_alive() for t in threads)
+        assert not bad, bad
