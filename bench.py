@@ -806,6 +806,16 @@ def run_ours(args) -> int:
     step_ms = max_over_ranks(step_ms, world, device)
     gemm_avg = max_over_ranks(gemm_avg, world, device)
     fc2_avg = max_over_ranks(fc2_avg, world, device)
+    # where the step's time goes: the events around the four launches (the
+    # fused reduce-scatter runs inside fc2's launch; an NCCL reduction comes
+    # after it), mean over the timed steps, max over ranks per phase
+    phases = {"quant_x": [s.elapsed_time(ev[0]) for s, ev in zip(starts, gemm_ev)],
+              "fc1_gelu": fc1_ms,
+              "quant_h": [ev[1].elapsed_time(ev[2]) for ev in gemm_ev],
+              "fc2": fc2_ms,
+              "after_fc2": [ev[3].elapsed_time(e) for ev, e in zip(gemm_ev, ends)]}
+    breakdown = {name: round(max_over_ranks(sum(v) / K, world, device), 4)
+                 for name, v in phases.items()}
     total_ops = mlp.int8_ops
     value = total_ops / (step_ms * 1e-3) / 1e12
 
@@ -959,6 +969,7 @@ def run_ours(args) -> int:
                                   "write); N > 1: each "
                                   "rank uploads its row slice, NCCL all-gather of the input"},
             "gpu_launches": K * launches,
+            "step_breakdown_ms": breakdown,
             "wall_s_timed_region": wall,
             "extras": extras,
         }
