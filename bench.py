@@ -948,6 +948,10 @@ def run_ours(args) -> int:
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_int8,
                          "unit": "TOPS", "frac": achieved / peak_int8, "traffic": traffic,
                          "kernel": "gemm_i8_pair_kernel<256,6,bf16> (fc1 and fc2 launches)",
+                         "traffic_source": "ncu dram__bytes_read + dram__bytes_write per launch, "
+                                           "mean of fc1 and fc2, from the one-GPU capture "
+                                           "summarised in profiles/gemm_i8_pair_mlp480p.md "
+                                           "(taken at commit d353045)",
                          "peak_source": f"2 x {peaks['source']} bf16 dense "
                                         f"({peaks['bf16_tflops']:.0f} TFLOP/s, MEASURED_PEAKS.json): "
                                         "sm_100 int8 tensor rate is twice bf16",
