@@ -126,8 +126,11 @@ int tm_cutlass_scaled_mm(void* out, int out_dtype, const int8_t* a, const int8_t
  * tm_cutlass_scaled_mm plus fused epilogue options (TM_EPI_* flags) and an
  * optional raw int32 accumulator output acc_debug[m, n] (row stride n), which
  * exposes the exact int32 sums for bit-exact checking.
- * Extends cutlass_scaled_mm for the BASELINE fc1 epilogue (bias + gelu_tanh);
- * no single reference call site.
+ * Replaces cutlass_scaled_mm (src/taomate_hd/inference/w8a8.py:72) followed by
+ * the activation: TM_EPI_SWIGLU is the merged fc1 and fused_swiglu
+ * (src/taomate_hd/inference/fused_kernels.py:298-309, called at
+ * src/taomate_hd/model/layers.py:525-533); TM_EPI_GELU_TANH is the BASELINE
+ * configuration's fc1 (bias + GELU-tanh), which has no reference call site.
  */
 int tm_scaled_mm_i8_ex(void* out, int out_dtype, const int8_t* a, const int8_t* b,
                        const float* scale_a, int64_t scale_a_numel, const float* scale_b,
